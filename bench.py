@@ -1,0 +1,476 @@
+#!/usr/bin/env python
+"""Benchmark of the paged-decode hot path on B200.
+
+Workload (default): Llama-3-8B attention shape, FP16, 32 query / 8 KV heads,
+head_dim 128, 32 layers, block 16, batch 256, lengths lognormal(median 1024,
+sigma 0.8) clipped to [16, 8192], RoPE theta 5e5, fragmented block tables,
+sequences sharded evenly over the ranks (each rank owns its pools/tables).
+
+One step = one decode token for every sequence through all 32 layers'
+attention ops: rope_kv_write (RoPE + paged KV-slot write) then paged_attention.
+Metric: seq-steps/s (sequences advanced one token through all layers per
+second), whole job. Inputs (60 GB of KV pools at batch 256) are far larger
+than L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU)
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+PKG = importlib.import_module("distributed-llm-inference_b200")
+W = importlib.import_module("distributed-llm-inference_b200.workloads")
+
+METRIC = "paged-attn decode seq-steps/s"
+UNIT = "seq-steps/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16"], default="llama3_8b")
+    ap.add_argument("--batch", type=int, default=None, help="override the workload batch")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def make_workload(args):
+    if args.workload == "llama3_8b":
+        return W.llama3_8b(batch=args.batch or 256, layers=args.layers or 32)
+    return W.smollm_fp16(batch=args.batch or 64, layers=args.layers or 30)
+
+
+# --------------------------------------------------------------------------
+# clocks sampled during the timed region (NVML; reading only)
+# --------------------------------------------------------------------------
+REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+           0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+           0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+           0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        self.error = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode() if isinstance(bus, str) else bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - report, never fail the bench
+            self.error = f"nvml unavailable: {e}"
+            self._nvml = None
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in REASONS.items():
+                    if r & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception as e:  # noqa: BLE001
+                self.error = str(e)
+            time.sleep(self.period)
+
+    def start(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self) -> dict:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+               "samples": len(self.samples)}
+        if self.error:
+            out["note"] = self.error
+        return out
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int, device):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[device.index])
+
+
+# --------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------
+class DecodeStep:
+    """All layers of one decode step through the public ops, with
+    preallocated outputs so the step can be captured in a CUDA graph."""
+
+    def __init__(self, w, t):
+        self.w, self.t = w, t
+        self.q_out = [torch.empty_like(q) for q in t.q]
+        self.k_out = [torch.empty_like(k) for k in t.k]
+        self.out = [torch.empty_like(q) for q in t.q]
+
+    def prologue(self, layer):
+        t = self.t
+        PKG.rope_kv_write(t.q[layer], t.k[layer], t.v[layer], t.k_pools[layer], t.v_pools[layer],
+                          t.physical, t.offsets, t.positions, t.inv_freq,
+                          q_out=self.q_out[layer], k_out=self.k_out[layer])
+
+    def attention(self, layer):
+        t = self.t
+        PKG.paged_attention(self.q_out[layer], t.k_pools[layer], t.v_pools[layer], t.tables,
+                            t.lengths, self.w.max_length, out=self.out[layer])
+
+    def __call__(self):
+        for layer in range(self.w.layers):
+            self.prologue(layer)
+            self.attention(layer)
+
+
+def capture(fn, stream):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+def time_graph(g, reps, stream):
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        s.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e)
+
+
+def e2e_run(w, t, steps, warmup, device):
+    """Public-API path with host buffers: every step copies each layer's new
+    q/k/v (and the step's tables/lengths/positions/slots) from pinned host
+    memory, runs rope_kv_write + paged_attention, and copies each layer's
+    attention output back to pinned host memory. Copies of layer l+1 overlap
+    the kernels of layer l (separate copy streams, event ordering)."""
+    L = w.layers
+    pin = lambda x: x.cpu().pin_memory()  # noqa: E731
+    h_q = [pin(x) for x in t.q]
+    h_k = [pin(x) for x in t.k]
+    h_v = [pin(x) for x in t.v]
+    h_meta = [pin(x) for x in (t.tables, t.lengths, t.positions, t.physical, t.offsets)]
+    h_out = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in t.q]
+    d_q = [torch.empty_like(x) for x in t.q]
+    d_k = [torch.empty_like(x) for x in t.k]
+    d_v = [torch.empty_like(x) for x in t.v]
+    d_meta = [torch.empty_like(x) for x in (t.tables, t.lengths, t.positions, t.physical, t.offsets)]
+    q_out = [torch.empty_like(x) for x in t.q]
+    k_out = [torch.empty_like(x) for x in t.k]
+    d_out = [torch.empty_like(x) for x in t.q]
+    comp = torch.cuda.current_stream(device)
+    h2d = torch.cuda.Stream(device)
+    d2h = torch.cuda.Stream(device)
+    copied = [torch.cuda.Event() for _ in range(L + 1)]
+    done = [torch.cuda.Event() for _ in range(L)]
+    h2d_bytes = sum(x.numel() * x.element_size() for x in h_q + h_k + h_v + h_meta)
+    d2h_bytes = sum(x.numel() * x.element_size() for x in h_out)
+
+    def step():
+        with torch.cuda.stream(h2d):
+            h2d.wait_stream(comp)  # previous step's kernels no longer read the buffers
+            for dm, hm in zip(d_meta, h_meta):
+                dm.copy_(hm, non_blocking=True)
+            copied[L].record(h2d)
+            for layer in range(L):
+                d_q[layer].copy_(h_q[layer], non_blocking=True)
+                d_k[layer].copy_(h_k[layer], non_blocking=True)
+                d_v[layer].copy_(h_v[layer], non_blocking=True)
+                copied[layer].record(h2d)
+        comp.wait_event(copied[L])
+        tables, lengths, positions, physical, offsets = d_meta
+        for layer in range(L):
+            comp.wait_event(copied[layer])
+            PKG.rope_kv_write(d_q[layer], d_k[layer], d_v[layer], t.k_pools[layer],
+                              t.v_pools[layer], physical, offsets, positions, t.inv_freq,
+                              q_out=q_out[layer], k_out=k_out[layer])
+            PKG.paged_attention(q_out[layer], t.k_pools[layer], t.v_pools[layer], tables, lengths,
+                                w.max_length, out=d_out[layer])
+            done[layer].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done[layer])
+                h_out[layer].copy_(d_out[layer], non_blocking=True)
+        comp.wait_stream(d2h)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(comp)
+    for _ in range(steps):
+        step()
+    e.record(comp)
+    e.synchronize()
+    ms = s.elapsed_time(e) / steps
+    check = float(h_out[-1].float().abs().sum())  # the step's result, read on the host
+    return ms, h2d_bytes, d2h_bytes, check
+
+
+def cpu_baseline(w, t, budget_s=20.0, sample=32):
+    """The reference's CPU path (oracle port of worker/llama.py:108-117,
+    :171-172, :58-71) on `sample` sequences of layer 0, all host threads,
+    padded to the batch max_length like the reference; scaled to seq-steps/s
+    over all layers."""
+    sys.path.insert(0, str(REPO))
+    from oracle import kv_cache, paged_attention as opa, rope as orope
+    idx = torch.arange(min(sample, w.batch))
+    tabs, (kp, vp) = W.compact_pages(w.tables[idx], w.lengths[idx], [t.k_pools[0], t.v_pools[0]],
+                                     w.block_size)
+    q = t.q[0][: len(idx)].cpu()
+    k = t.k[0][: len(idx)].cpu()
+    v = t.v[0][: len(idx)].cpu()
+    lens = w.lengths[idx]
+    pos = (lens.to(torch.int64) - 1).unsqueeze(1)
+    phys = tabs.to(torch.int64).gather(1, (pos // w.block_size))[:, 0]
+    off = pos[:, 0] % w.block_size
+    inv = t.inv_freq.cpu()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or not times:
+        t0 = time.perf_counter()
+        qr, kr = orope.rope(q.unsqueeze(1), k.unsqueeze(1), pos, inv)
+        kv_cache.write_decode(kp, phys, off, kr[:, 0])
+        kv_cache.write_decode(vp, phys, off, v)
+        opa.paged_attention(qr[:, 0], kp, vp, tabs, lens, w.max_length)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 5:
+            break
+    per_layer = statistics.median(times)
+    return {"value": len(idx) / (per_layer * w.layers), "unit": UNIT,
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(idx)} of {w.batch} sequences x layer 0, scaled by {w.layers} layers "
+                      f"(all layers have the same shapes); padded to max_length {w.max_length} "
+                      f"like the reference; median of {len(times)} runs; os.cpu_count()={os.cpu_count()}"}
+
+
+def run_ours(args):
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    PKG.load_library()
+    full = make_workload(args)
+    w = full.shard(rank, world) if world > 1 else full
+    t = W.materialize(w, device)
+    step = DecodeStep(w, t)
+    stream = torch.cuda.Stream(device)
+
+    # warm caches (occupancy, workspace) on the capture stream, then capture
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize(device)
+    g_step = capture(step, stream)
+    g_attn = capture(lambda: [step.attention(i) for i in range(w.layers)], stream)
+    g_pro = capture(lambda: [step.prologue(i) for i in range(w.layers)], stream)
+
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    for _ in range(args.warmup):
+        with torch.cuda.stream(stream):
+            g_step.replay()
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    torch.cuda.synchronize(device)
+    ms_total = time_graph(g_step, args.steps, stream)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    clk = clocks.stop()
+    ms_total = max_over_ranks(ms_total, world, device)
+    ms_step = ms_total / args.steps
+
+    # roofline of the dominant kernel: attention launches alone, same inputs
+    reps = max(3, min(20, args.steps))
+    ms_attn = time_graph(g_attn, reps, stream) / (reps * w.layers)
+    ms_pro = time_graph(g_pro, reps, stream) / (reps * w.layers)
+    attn_bytes = w.attention_bytes()
+    peaks = {}
+    pk = REPO / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    peak = peaks.get("hbm_gbs")
+    peak_src = "measured" if peak else "fallback"
+    peak = peak or 6650.0
+    achieved = attn_bytes / (ms_attn * 1e-3) / 1e9
+    traffic = None
+    tf = REPO / "profiles" / "traffic.json"
+    if tf.exists():
+        tj = json.loads(tf.read_text())
+        if tj.get("workload") == full.name and tj.get("world") == world:
+            traffic = tj.get("bytes_per_launch")
+
+    e2e = None
+    if not args.no_e2e:
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        ms_e2e, h2d, d2h, _ = e2e_run(w, t, args.steps, args.warmup, device)
+        barrier(world, device)
+        ms_e2e = max_over_ranks(ms_e2e, world, device)
+        e2e = {"value": full.batch / (ms_e2e * 1e-3), "unit": UNIT, "ms_per_step": ms_e2e,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "public ops with pinned host buffers, H2D/D2H on copy streams"}
+
+    # output checksum across ranks (outside every timed region)
+    chk = torch.tensor([float(sum(o.float().abs().sum() for o in step.out))], device=device,
+                       dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(chk)
+
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline(w, t)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": full.batch / (ms_step * 1e-3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic (seeded; no dataset in this path)",
+            "config": {
+                "workload": f"{full.name}: batch {full.batch}, {full.heads}/{full.kv_heads} heads, "
+                            f"head_dim {full.head_dim}, {full.layers} layers, block {full.block_size}, "
+                            f"lengths lognormal(1024, 0.8) in [16, 8192]"
+                            if args.workload == "llama3_8b" else full.name,
+                "batch": full.batch, "layers": full.layers, "max_length": full.max_length,
+                "mean_length": float(full.lengths.float().mean()),
+                "sharding": "sequences split evenly over ranks; each rank owns its pools",
+                "l2": "inputs larger than L2 (KV pools %.1f GB per rank)" % (
+                    2 * w.layers * w.num_blocks * w.block_size * w.kv_heads * w.head_dim
+                    * w.elem_bytes / 1e9),
+                "step": "per layer: rope_kv_write + paged_attention, one CUDA graph per step",
+            },
+            "algorithmic_gb_per_step": full.seq_step_bytes() / 1e9,
+            "achieved_gbs_step": full.seq_step_bytes() / (ms_step * 1e-3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "attn_fast_kernel", "peak_source": f"{peak_src} hbm_gbs",
+                         "algorithmic_bytes_per_launch": attn_bytes,
+                         "ms_per_launch": ms_attn, "prologue_ms_per_launch": ms_pro},
+            "clocks": clk,
+            "gpu_launches": args.steps * w.layers * 2,
+            "e2e": e2e,
+            "cpu_baseline": base,
+            "checksum": float(chk.item()),
+        }
+        print(json.dumps(line), flush=True)
+    del g_step, g_attn, g_pro
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[device.index])
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference's own CPU implementation of the path (oracle port of
+    worker/llama.py:58-71, :108-117, :171-172; the reference compiles no
+    CPU code) on the host cores, same workload/metric. Each step is a
+    bounded sample: 8 sequences of one layer, scaled to seq-steps/s."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import kv_cache, paged_attention as opa, rope as orope
+    torch.set_num_threads(os.cpu_count() or 1)
+    full = make_workload(args)
+    n = min(8, full.batch)
+    tabs, blocks, used = W.make_decode_tables(full.lengths[:n], full.block_size, full.seed, 1.25, None)
+    # pad the sample's tables to the batch's width, as TensorPagedKV.metadata does
+    wide = torch.zeros(n, full.table_width, dtype=torch.int32)
+    wide[:, :tabs.shape[1]] = tabs
+    sub = W.DecodeWorkload(full.name, n, full.heads, full.kv_heads, full.head_dim, 1,
+                           full.block_size, full.dtype, full.theta, full.seed, full.lengths[:n],
+                           wide, blocks, used, stale_scale=full.stale_scale)
+    t = W.materialize(sub, "cpu")
+    pos = sub.positions()
+    phys, off = sub.slots()
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        qr, kr = orope.rope(t.q[0].unsqueeze(1), t.k[0].unsqueeze(1), pos, t.inv_freq)
+        kv_cache.write_decode(t.k_pools[0], phys, off, kr[:, 0])
+        kv_cache.write_decode(t.v_pools[0], phys, off, t.v[0])
+        opa.paged_attention(qr[:, 0], t.k_pools[0], t.v_pools[0], sub.tables, sub.lengths,
+                            full.max_length)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times) * full.layers  # one step of the sample, all layers
+    value = n / sec
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3 * full.batch / n,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": full.name, "batch": full.batch, "layers": full.layers,
+                       "max_length": full.max_length},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                             "kind": "port",
+                             "sample": f"{n} of {full.batch} sequences x 1 layer per step, scaled by "
+                                       f"{full.layers} layers; padded to max_length {full.max_length}"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,21 @@
+"""Blackwell (sm_100a) paged-decode hot path of sri123vk/distributed-llm-inference.
+
+Public ops (drop-in for the reference's decode path):
+  paged_attention(q, k, v, tables, lengths, max_length)   cuda/binding.cpp:6-26
+  rope_kv_write(q, k, v, k_pool, v_pool, physical, offsets, positions, inv_freq[, valid])
+      worker/llama.py:108-117 + :171-172 (decode) / :139-140 (prefill)
+  cuda_paged_attention(...)  the reference loader's name (worker/llama.py:77-86)
+  install(llama_module)      points a worker.llama module at these ops
+
+The package directory name contains '-', so import it with
+importlib.import_module("distributed-llm-inference_b200").
+"""
+from ._lib import IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, load as load_library  # noqa: F401
+from .ops import fast_grid_size, paged_attention, read_device_errors, rope_kv_write  # noqa: F401
+from .integration import cuda_paged_attention, install  # noqa: F401
+
+__all__ = [
+    "paged_attention", "rope_kv_write", "cuda_paged_attention", "install",
+    "read_device_errors", "fast_grid_size", "load_library",
+    "IMPL_AUTO", "IMPL_FAST", "IMPL_GENERIC",
+]

@@ -1,0 +1,411 @@
+// C ABI of libpaged_decode_b200.so: argument checks, kernel selection,
+// workspace layout and launches. Declarations: include/paged_decode_b200.h.
+//
+// All kernels are compiled in this one translation unit (the headers below),
+// so the per-device error word is a single __device__ variable.
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+
+#include "../../include/paged_decode_b200.h"
+#include "attention.cuh"
+#include "rope_kv_write.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return PDB_ERR_CUDA;
+}
+
+// ---- per-device facts -------------------------------------------------------
+std::mutex g_mu;
+
+int sm_count(int dev) {
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 0;
+  cache[dev] = n;
+  return n;
+}
+
+// Occupancy (CTAs per SM) of `fn` with `smem` dynamic bytes on `dev`; also
+// raises the function's dynamic shared-memory limit on first use.
+int ctas_per_sm(int dev, const void* fn, size_t smem, int threads) {
+  static std::map<std::tuple<int, const void*, size_t>, int> cache;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto key = std::make_tuple(dev, fn, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    cache[key] = 0;
+    return 0;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+std::atomic<uint32_t> g_epoch{1};
+uint32_t next_epoch() {
+  uint32_t e = g_epoch.fetch_add(1);
+  if (e == 0) e = g_epoch.fetch_add(1);  // 0 marks never-used counters
+  return e;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---- fast kernel registry ---------------------------------------------------
+struct FastKernel {
+  const void* fn;
+  void (*launch)(const pdb::AttnParams&, int grid, size_t smem, cudaStream_t);
+  size_t (*smem)(int B);
+  int gp;
+};
+
+template <class Tr>
+void launch_fast(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st) {
+  pdb::attn_fast_kernel<Tr><<<grid, Tr::NT, smem, st>>>(p);
+}
+
+template <class Tr>
+FastKernel make_fast() {
+  return FastKernel{reinterpret_cast<const void*>(&pdb::attn_fast_kernel<Tr>), &launch_fast<Tr>,
+                    &Tr::smem_bytes, Tr::GP};
+}
+
+// Tile depth per (dtype, head_dim): ~16 KB (fp16) / 32 KB (fp32) stages.
+template <typename T, int D, int GP>
+FastKernel fast_for() {
+  if constexpr (sizeof(T) == 2) {
+    if constexpr (D == 128) return make_fast<pdb::FastTraits<T, D, GP, 2, 4>>();
+    else return make_fast<pdb::FastTraits<T, D, GP, 2, 6>>();
+  } else {
+    if constexpr (D == 128) return make_fast<pdb::FastTraits<T, D, GP, 2, 3>>();
+    else if constexpr (D == 64) return make_fast<pdb::FastTraits<T, D, GP, 2, 4>>();
+    else return make_fast<pdb::FastTraits<T, D, GP, 2, 6>>();
+  }
+}
+
+template <typename T, int D>
+bool pick_gp(int G, FastKernel* out) {
+  if (G <= 1) { *out = fast_for<T, D, 1>(); return true; }
+  if (G <= 2) { *out = fast_for<T, D, 2>(); return true; }
+  if (G <= 4) { *out = fast_for<T, D, 4>(); return true; }
+  if constexpr (D <= 64) {
+    if (G <= 8) { *out = fast_for<T, D, 8>(); return true; }
+  }
+  return false;
+}
+
+template <typename T>
+bool pick_fast_t(int D, int G, FastKernel* out) {
+  switch (D) {
+    case 32: return pick_gp<T, 32>(G, out);
+    case 64: return pick_gp<T, 64>(G, out);
+    case 128: return pick_gp<T, 128>(G, out);
+    default: return false;
+  }
+}
+
+constexpr int kFastMaxBatch = 4096;
+
+bool fast_applicable(int64_t B, int64_t H, int64_t KVH, int64_t D, int dtype, FastKernel* k) {
+  if (B > kFastMaxBatch) return false;
+  if (B * KVH * (8192 / pdb::kUnitTokens) >= (int64_t(1) << 31)) return false;
+  const int G = (int)(H / KVH);
+  return dtype == PDB_DTYPE_FLOAT16 ? pick_fast_t<__half>((int)D, G, k)
+                                    : pick_fast_t<float>((int)D, G, k);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Grid of the fast kernel: one wave of resident CTAs, but never more CTAs
+// than the upper bound on 16-token units.
+int64_t fast_grid(int dev, const FastKernel& k, int64_t B, int64_t KVH, int64_t max_length) {
+  const size_t smem = k.smem((int)B);
+  const int occ = ctas_per_sm(dev, k.fn, smem, 128);
+  const int sms = sm_count(dev);
+  if (occ <= 0 || sms <= 0) return 0;
+  int64_t grid = (int64_t)occ * sms;
+  const int64_t units = B * KVH * ((max_length + pdb::kUnitTokens - 1) / pdb::kUnitTokens);
+  if (grid > units) grid = units;
+  return grid < 1 ? 1 : grid;
+}
+
+struct FastWs {
+  size_t counters_off, partials_off, total;
+};
+FastWs fast_ws_layout(int64_t B, int64_t KVH, int64_t D, int gp, int64_t grid) {
+  FastWs w;
+  w.counters_off = 0;
+  w.partials_off = align256((size_t)(B * KVH) * sizeof(unsigned long long));
+  w.total = w.partials_off + align256((size_t)(2 * grid) * gp * (D + 2) * sizeof(float));
+  return w;
+}
+
+int generic_splits(int64_t max_length) {
+  int64_t s = (max_length + 511) / 512;
+  if (s < 1) s = 1;
+  if (s > 16) s = 16;
+  return (int)s;
+}
+size_t generic_ws(int64_t B, int64_t H, int64_t D, int splits) {
+  return splits > 1 ? align256((size_t)(B * H * splits) * (D + 2) * sizeof(float)) : 0;
+}
+
+int check_attention_args(int64_t B, int64_t H, int64_t D, int64_t N, int64_t bs, int64_t KVH,
+                         int64_t Dk, int64_t W, int64_t max_length, int dtype) {
+  // Messages and order of cuda/binding.cpp:14-22.
+  if (!(B > 0 && H > 0 && D > 0 && D <= 256))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid query shape");
+  if (!(N > 0 && bs > 0 && KVH > 0 && Dk == D))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid cache shape");
+  if (H % KVH != 0)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "query heads must be a multiple of KV heads");
+  if (dtype != PDB_DTYPE_FLOAT32 && dtype != PDB_DTYPE_FLOAT16)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "use FP32 or FP16");
+  if (W < 0) return fail(PDB_ERR_INVALID_ARGUMENT, "invalid block tables");
+  if (!(max_length > 0 && max_length <= 8192 && W * bs >= max_length))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid context bound");
+  if (B > INT32_MAX || H > INT32_MAX || N > INT64_MAX / (bs * KVH * D) ||
+      W > INT32_MAX || bs > INT32_MAX)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "shape too large");
+  return PDB_OK;
+}
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  return PDB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pdb_last_error(void) { return g_last_error.c_str(); }
+
+const char* pdb_version(void) { return "paged_decode_b200 0.1 (sm_100a)"; }
+
+size_t pdb_paged_attention_workspace_size(int64_t batch, int64_t heads, int64_t kv_heads,
+                                          int64_t head_dim, int64_t max_length, int dtype) {
+  if (batch <= 0 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || heads % kv_heads ||
+      max_length <= 0)
+    return 0;
+  size_t need = generic_ws(batch, heads, head_dim, generic_splits(max_length));
+  FastKernel k;
+  int dev = 0;
+  if (fast_applicable(batch, heads, kv_heads, head_dim, dtype, &k) &&
+      cudaGetDevice(&dev) == cudaSuccess) {
+    const int64_t grid = fast_grid(dev, k, batch, kv_heads, max_length);
+    if (grid > 0) {
+      const size_t f = fast_ws_layout(batch, kv_heads, head_dim, k.gp, grid).total;
+      if (f > need) need = f;
+    }
+  }
+  return need;
+}
+
+int64_t pdb_fast_grid_size(int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                           int dtype) {
+  FastKernel k;
+  int dev = 0;
+  if (batch <= 0 || kv_heads <= 0 || heads % kv_heads) return 0;
+  if (!fast_applicable(batch, heads, kv_heads, head_dim, dtype, &k)) return 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  return fast_grid(dev, k, batch, kv_heads, 8192);
+}
+
+int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_pool,
+                             const int32_t* tables, const int32_t* lengths, void* out,
+                             int64_t B, int64_t H, int64_t D, int64_t N, int64_t bs,
+                             int64_t KVH, int64_t Dk, int64_t W, int64_t max_length,
+                             int dtype, void* workspace, size_t workspace_bytes, void* stream,
+                             int impl) {
+  int rc = check_attention_args(B, H, D, N, bs, KVH, Dk, W, max_length, dtype);
+  if (rc) return rc;
+  if (!q || !k_pool || !v_pool || !tables || !lengths || !out)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (impl < PDB_IMPL_AUTO || impl > PDB_IMPL_GENERIC)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "unknown kernel selection");
+  int dev = 0;
+  if ((rc = current_device(&dev))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  pdb::AttnParams p{};
+  p.q = q; p.k_pool = k_pool; p.v_pool = v_pool;
+  p.tables = tables; p.lengths = lengths; p.out = out;
+  p.B = (int)B; p.H = (int)H; p.KVH = (int)KVH; p.G = (int)(H / KVH); p.D = (int)D;
+  p.num_blocks = N; p.block_size = (int)bs;
+  p.bs_shift = ((bs & (bs - 1)) == 0) ? __builtin_ctzll((unsigned long long)bs) : -1;
+  p.table_width = (int)W;
+  p.max_length = (int)max_length;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
+
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(PDB_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+
+  FastKernel fk;
+  const bool fast_ok = fast_applicable(B, H, KVH, D, dtype, &fk) && aligned16(q) &&
+                       aligned16(k_pool) && aligned16(v_pool);
+  if (impl == PDB_IMPL_FAST && !fast_ok)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "fast kernel does not support this shape/alignment");
+
+  if (fast_ok && impl != PDB_IMPL_GENERIC) {
+    const int64_t grid = fast_grid(dev, fk, B, KVH, max_length);
+    if (grid <= 0) return fail(PDB_ERR_CUDA, "fast kernel cannot be resident on this device");
+    const FastWs ws = fast_ws_layout(B, KVH, D, fk.gp, grid);
+    if (!workspace || workspace_bytes < ws.total)
+      return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) +
+                                         " bytes");
+    unsigned char* wb = static_cast<unsigned char*>(workspace);
+    p.counters = reinterpret_cast<unsigned long long*>(wb + ws.counters_off);
+    p.partials = reinterpret_cast<float*>(wb + ws.partials_off);
+    p.epoch = next_epoch();
+    fk.launch(p, (int)grid, fk.smem((int)B), st);
+  } else {
+    const int splits = generic_splits(max_length);
+    const size_t need = generic_ws(B, H, D, splits);
+    if (need && (!workspace || workspace_bytes < need))
+      return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) +
+                                         " bytes");
+    p.splits = splits;
+    p.chunk = (int)((max_length + splits - 1) / splits);
+    p.partials = static_cast<float*>(workspace);
+    dim3 grid(splits, (unsigned)H, (unsigned)B);
+    if (dtype == PDB_DTYPE_FLOAT16) {
+      pdb::attn_generic_kernel<__half><<<grid, 128, 0, st>>>(p);
+      if (splits > 1) pdb::attn_combine_kernel<__half><<<dim3((unsigned)H, (unsigned)B), 128, 0, st>>>(p);
+    } else {
+      pdb::attn_generic_kernel<float><<<grid, 128, 0, st>>>(p);
+      if (splits > 1) pdb::attn_combine_kernel<float><<<dim3((unsigned)H, (unsigned)B), 128, 0, st>>>(p);
+    }
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention launch");
+  return PDB_OK;
+}
+
+int pdb_paged_attention(const void* q, const void* k_pool, const void* v_pool,
+                        const int32_t* tables, const int32_t* lengths, void* out, int64_t B,
+                        int64_t H, int64_t D, int64_t N, int64_t bs, int64_t KVH, int64_t Dk,
+                        int64_t W, int64_t max_length, int dtype, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return pdb_paged_attention_impl(q, k_pool, v_pool, tables, lengths, out, B, H, D, N, bs, KVH,
+                                  Dk, W, max_length, dtype, workspace, workspace_bytes, stream,
+                                  PDB_IMPL_AUTO);
+}
+
+size_t pdb_rope_kv_write_workspace_size(int64_t batch, int64_t seq, int has_valid) {
+  if (!has_valid || batch <= 0 || seq <= 0) return 0;
+  return align256((size_t)(batch * seq) * sizeof(int32_t));
+}
+
+int pdb_rope_kv_write(const void* q, const void* k, const void* v, void* q_out, void* k_out,
+                      void* k_pool, void* v_pool, const int64_t* positions,
+                      int64_t pos_stride_b, int64_t pos_stride_s, const float* inv_freq,
+                      const int64_t* physical, const int64_t* offsets, int64_t num_slots,
+                      const uint8_t* valid, int64_t batch, int64_t seq, int64_t heads,
+                      int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                      int64_t block_size, int dtype, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (!(batch > 0 && seq > 0 && heads > 0 && kv_heads > 0 && head_dim > 0))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid q/k/v shapes");
+  if (head_dim % 2)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "head_dim must be even for rotate-half RoPE");
+  if (!(num_blocks > 0 && block_size > 0))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid cache shape");
+  if (dtype != PDB_DTYPE_FLOAT32 && dtype != PDB_DTYPE_FLOAT16)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "use FP32 or FP16");
+  const int64_t rows = batch * seq;
+  if (num_slots < 0 || (!valid && num_slots != rows))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "number of slots must match the rows written");
+  if (rows > INT32_MAX || heads * head_dim > INT32_MAX || kv_heads * head_dim > INT32_MAX)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "shape too large");
+  if (!q || !k || !v || !q_out || !k_out || !k_pool || !v_pool || !positions || !inv_freq ||
+      (num_slots > 0 && (!physical || !offsets)))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  const int32_t* slot_of_row = nullptr;
+  if (valid) {
+    const size_t need = pdb_rope_kv_write_workspace_size(batch, seq, 1);
+    if (!workspace || workspace_bytes < need)
+      return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) +
+                                         " bytes");
+    int32_t* sor = static_cast<int32_t*>(workspace);
+    pdb::valid_scan_kernel<1024, 8><<<1, 1024, 0, st>>>(valid, rows, num_slots, sor);
+    slot_of_row = sor;
+  }
+  pdb::RopeParams p{};
+  p.q = q; p.k = k; p.v = v; p.q_out = q_out; p.k_out = k_out;
+  p.k_pool = k_pool; p.v_pool = v_pool;
+  p.positions = positions; p.pos_stride_b = pos_stride_b; p.pos_stride_s = pos_stride_s;
+  p.inv_freq = inv_freq; p.physical = physical; p.offsets = offsets;
+  p.slot_of_row = slot_of_row; p.num_slots = num_slots; p.seq = seq;
+  p.heads = (int)heads; p.kv_heads = (int)kv_heads; p.dim = (int)head_dim;
+  p.num_blocks = num_blocks; p.block_size = (int)block_size;
+  const size_t smem = (size_t)head_dim * sizeof(float);
+  if (dtype == PDB_DTYPE_FLOAT16)
+    pdb::rope_kv_write_kernel<__half><<<(unsigned)rows, 128, smem, st>>>(p);
+  else
+    pdb::rope_kv_write_kernel<float><<<(unsigned)rows, 128, smem, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rope_kv_write launch");
+  return PDB_OK;
+}
+
+int pdb_read_device_errors(uint32_t* flags, int clear) {
+  if (!flags) return fail(PDB_ERR_INVALID_ARGUMENT, "null output pointer");
+  unsigned v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  e = cudaMemcpyFromSymbol(&v, pdb::g_device_errors, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "read error word");
+  if (clear) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(pdb::g_device_errors, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "clear error word");
+  }
+  *flags = v;
+  return PDB_OK;
+}
+
+int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch, int64_t kv_heads,
+                            int64_t grid, int64_t* ranges) {
+  if (!lengths || !ranges || batch <= 0 || kv_heads <= 0 || grid <= 0) return -1;
+  int64_t U = 0;
+  for (int64_t b = 0; b < batch; ++b) {
+    const int64_t len = lengths[b] < 0 ? 0 : lengths[b];
+    U += kv_heads * ((len + pdb::kUnitTokens - 1) / pdb::kUnitTokens);
+  }
+  for (int64_t c = 0; c < grid; ++c) {
+    ranges[2 * c] = pdb::part_begin(c, U, grid);
+    ranges[2 * c + 1] = pdb::part_begin(c + 1, U, grid);
+  }
+  return U;
+}
+
+}  // extern "C"

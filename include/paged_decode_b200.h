@@ -1,0 +1,180 @@
+/*
+ * paged_decode_b200.h — C ABI of the sm_100a paged-decode library
+ * (libpaged_decode_b200.so).
+ *
+ * The library replaces the decode hot path of
+ * sri123vk/distributed-llm-inference:
+ *   - the `paged_attention` torch extension op (cuda/binding.cpp:6-30,
+ *     kernel cuda/paged_attention.cu:10-74), and
+ *   - the per-token RoPE + paged KV-slot write that worker/llama.py performs
+ *     in PyTorch (worker/llama.py:105-117 RoPE, :171-172 decode slot write,
+ *     :138-140 prefill slot write).
+ *
+ * Conventions shared by every entry point:
+ *   - Plain device pointers and sizes; no framework types. Tensors are dense,
+ *     row-major ("contiguous") with the shapes given per argument.
+ *   - `dtype` is a pdb_dtype_t. q, k, v, pools and outputs share it.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). All work is
+ *     enqueued asynchronously on it; no entry point synchronises.
+ *   - Return value is a pdb_status_t. On failure pdb_last_error() returns a
+ *     message (thread-local) and nothing was enqueued. The argument checks and
+ *     their messages are those of cuda/binding.cpp:8-22.
+ *   - Inputs are borrowed; outputs and pools are written in place.
+ *   - Device-side validation (table entries, lengths, slots) never faults: a
+ *     bad entry is skipped and a bit is set in a per-device error word that
+ *     pdb_read_device_errors() returns.
+ */
+#ifndef PAGED_DECODE_B200_H
+#define PAGED_DECODE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PDB_API __attribute__((visibility("default")))
+#else
+#define PDB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  PDB_DTYPE_FLOAT32 = 0,
+  PDB_DTYPE_FLOAT16 = 1
+} pdb_dtype_t;
+
+typedef enum {
+  PDB_OK = 0,
+  PDB_ERR_INVALID_ARGUMENT = 1, /* reference: TORCH_CHECK failure          */
+  PDB_ERR_WORKSPACE = 2,        /* workspace missing, too small or misaligned */
+  PDB_ERR_CUDA = 3              /* reference: C10_CUDA_KERNEL_LAUNCH_CHECK  */
+} pdb_status_t;
+
+/* Kernel selection for pdb_paged_attention_impl. */
+typedef enum {
+  PDB_IMPL_AUTO = 0,    /* fast kernel when the shape allows, else generic   */
+  PDB_IMPL_FAST = 1,    /* GQA-shared, cp.async-staged, stream-K split       */
+  PDB_IMPL_GENERIC = 2  /* any head_dim <= 256 / any alignment, split + combine */
+} pdb_impl_t;
+
+/* Bits of the per-device error word (pdb_read_device_errors). */
+#define PDB_DEVERR_TABLE_ENTRY 0x1u  /* block-table entry outside [0, num_blocks) */
+#define PDB_DEVERR_LENGTH 0x2u       /* length < 0 or > table_width*block_size   */
+#define PDB_DEVERR_SLOT 0x4u         /* KV slot outside the pool                  */
+#define PDB_DEVERR_VALID_COUNT 0x8u  /* valid-row count != number of slots        */
+
+/* Thread-local message of the last failed call ("" if none). */
+PDB_API const char* pdb_last_error(void);
+
+/* Library version string. */
+PDB_API const char* pdb_version(void);
+
+/*
+ * Bytes of device workspace that pdb_paged_attention needs for this shape on
+ * the current device (0 is a valid answer). The workspace is scratch: its
+ * contents need not be preserved between calls, but calls that overlap on the
+ * GPU must not share one. It must be 256-byte aligned.
+ */
+PDB_API size_t pdb_paged_attention_workspace_size(int64_t batch, int64_t heads,
+                                          int64_t kv_heads, int64_t head_dim,
+                                          int64_t max_length, int dtype);
+
+/*
+ * Paged GQA decode attention.
+ * Replaces: paged_attention(q, k, v, tables, lengths, max_length)
+ *           cuda/binding.cpp:6-26 and cuda/paged_attention.cu:60-74.
+ *   q       [batch, heads, head_dim]
+ *   k_pool  [num_blocks, block_size, kv_heads, kv_head_dim]   (v_pool same)
+ *   tables  int32 [batch, table_width]   physical block of page i of seq b
+ *   lengths int32 [batch]                tokens to attend per sequence
+ *   out     [batch, heads, head_dim]     softmax(q K^T / sqrt(head_dim)) V,
+ *                                        0 for a zero-length sequence
+ * Checks (messages of cuda/binding.cpp:12-22): batch, heads, head_dim > 0,
+ * head_dim <= 256; num_blocks, block_size, kv_heads > 0 and
+ * kv_head_dim == head_dim; heads % kv_heads == 0; dtype FP32/FP16;
+ * 0 < max_length <= 8192 and table_width*block_size >= max_length.
+ * The caller guarantees 0 <= lengths[b] <= max_length (cuda/binding.cpp:23-24).
+ */
+PDB_API int pdb_paged_attention(const void* q, const void* k_pool, const void* v_pool,
+                        const int32_t* tables, const int32_t* lengths, void* out,
+                        int64_t batch, int64_t heads, int64_t head_dim,
+                        int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                        int64_t kv_head_dim, int64_t table_width,
+                        int64_t max_length, int dtype, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* Same as pdb_paged_attention with an explicit kernel choice (pdb_impl_t).
+ * No reference counterpart: used by tests to pin each kernel separately. */
+PDB_API int pdb_paged_attention_impl(const void* q, const void* k_pool,
+                             const void* v_pool, const int32_t* tables,
+                             const int32_t* lengths, void* out, int64_t batch,
+                             int64_t heads, int64_t head_dim, int64_t num_blocks,
+                             int64_t block_size, int64_t kv_heads,
+                             int64_t kv_head_dim, int64_t table_width,
+                             int64_t max_length, int dtype, void* workspace,
+                             size_t workspace_bytes, void* stream, int impl);
+
+/*
+ * Fused RoPE + paged KV-slot write (the prologue of one attention layer).
+ * Replaces: PagedLlama.rope (worker/llama.py:108-117) followed by
+ *           keys[layer][slots] = k ; values[layer][slots] = v
+ *           (decode worker/llama.py:170-172, prefill :138-140).
+ *   q, q_out   [rows, heads, head_dim]      (q_out may alias q)
+ *   k, k_out   [rows, kv_heads, head_dim]   (k_out may alias k)
+ *   v          [rows, kv_heads, head_dim]
+ *   rows = batch * seq; row r is (r / seq, r % seq).
+ *   positions  int64, position of row r = positions[(r/seq)*pos_stride_b +
+ *              (r%seq)*pos_stride_s] (strides in elements; 0 broadcasts).
+ *   inv_freq   fp32 [head_dim/2]   (worker/llama.py:105-106, computed by the
+ *              caller so that both sides use identical frequencies)
+ *   physical, offsets  int64 [num_slots]  slot j = (block, offset in block)
+ *   valid      uint8 [rows] or NULL. NULL: row r writes slot r (decode,
+ *              num_slots == rows). Otherwise the j-th valid row in row-major
+ *              order writes slot j (the `pool[slots] = k[valid]` of prefill).
+ *   k_pool, v_pool [num_blocks, block_size, kv_heads, head_dim]
+ * Rounding follows the reference op by op: angles fp32, cos/sin rounded to
+ * dtype, then x*cos and rotate(x)*sin each rounded to dtype, then their sum.
+ */
+PDB_API int pdb_rope_kv_write(const void* q, const void* k, const void* v, void* q_out,
+                      void* k_out, void* k_pool, void* v_pool,
+                      const int64_t* positions, int64_t pos_stride_b,
+                      int64_t pos_stride_s, const float* inv_freq,
+                      const int64_t* physical, const int64_t* offsets,
+                      int64_t num_slots, const uint8_t* valid, int64_t batch,
+                      int64_t seq, int64_t heads, int64_t kv_heads,
+                      int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                      int dtype, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* Workspace bytes pdb_rope_kv_write needs (0 when valid is NULL). */
+PDB_API size_t pdb_rope_kv_write_workspace_size(int64_t batch, int64_t seq,
+                                        int has_valid);
+
+/*
+ * Reads (and optionally clears) the error word of the current device.
+ * Synchronises the device. No reference counterpart: the reference kernel
+ * does not validate table entries or lengths on the device.
+ */
+PDB_API int pdb_read_device_errors(uint32_t* flags, int clear);
+
+/*
+ * Host-side copy of the fast kernel's work partition, for tests. No
+ * reference counterpart. For each of `grid` CTAs writes into ranges[2*c] and
+ * ranges[2*c+1] its [begin, end) in 16-token units over the sequence of
+ * (sequence, kv_head) segments; returns the total unit count or -1.
+ */
+PDB_API int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch,
+                            int64_t kv_heads, int64_t grid, int64_t* ranges);
+
+/* CTAs the fast kernel launches per call on the current device for this
+ * shape (0 when the fast kernel does not apply). No reference counterpart. */
+PDB_API int64_t pdb_fast_grid_size(int64_t batch, int64_t heads, int64_t kv_heads,
+                           int64_t head_dim, int dtype);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGED_DECODE_B200_H */

@@ -1,0 +1,196 @@
+"""Generate the golden fixtures of tests/golden/ from the REFERENCE's own code.
+
+Run in a container that has the reference checkout (read-only) at
+/root/reference:
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [/path/to/reference]
+
+It imports worker.llama (torch_paged_attention, PagedLlama.rope) and
+worker.engine (PagedKV) from the reference, feeds them the seeded inputs of
+the package's workloads module (CPU generators, deterministic), and saves the
+reference's outputs, plus SHA-256 digests of the inputs so that a drift of
+the input generators is detected. The fixtures travel with the repository;
+the reference itself does not.
+"""
+from __future__ import annotations
+
+import hashlib
+import importlib
+import math
+import sys
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO))
+W = importlib.import_module("distributed-llm-inference_b200.workloads")
+
+
+def digest(t: torch.Tensor) -> str:
+    return hashlib.sha256(t.detach().contiguous().cpu().view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+class _RopeHost:
+    """Stand-in `self` for the unbound PagedLlama.rope (it only reads inv_freq)."""
+
+    def __init__(self, inv_freq):
+        self.inv_freq = inv_freq
+
+
+def edge_case_specs():
+    """Small decode cases covering the reference's edge cases: zero length,
+    length 1, page-boundary lengths, non-power-of-two block sizes, MHA / GQA /
+    MQA groupings, several head dims, fp32 and fp16."""
+    specs = []
+    shapes = [
+        # (B, H, KVH, D, bs)
+        (7, 4, 2, 32, 16),
+        (7, 9, 3, 64, 16),
+        (7, 8, 8, 64, 16),     # MHA
+        (7, 8, 1, 64, 16),     # MQA, group 8
+        (7, 32, 8, 128, 16),
+        (7, 4, 4, 128, 8),
+        (7, 6, 2, 40, 5),      # odd block size, head_dim not a multiple of 32
+        (7, 2, 1, 256, 16),
+        (7, 16, 2, 128, 16),   # group 8 at D=128
+    ]
+    for dtype in ("float32", "float16"):
+        for i, (B, H, KVH, D, bs) in enumerate(shapes):
+            lengths = [0, 1, bs - 1, bs, bs + 1, 2 * bs + 3, 70]
+            specs.append(dict(name=f"{dtype}-{i}", dtype=dtype, B=B, H=H, KVH=KVH, D=D, bs=bs,
+                              lengths=lengths, seed=1000 + i))
+    return specs
+
+
+def edge_case_inputs(spec):
+    dtype = getattr(torch, spec["dtype"])
+    g = torch.Generator().manual_seed(spec["seed"])
+    lengths = torch.tensor(spec["lengths"], dtype=torch.int32)
+    bs = spec["bs"]
+    need = sum(math.ceil(n / bs) for n in spec["lengths"])
+    blocks = need + 5
+    max_len = max(spec["lengths"])
+    width = math.ceil(max_len / bs)
+    perm = torch.randperm(blocks, generator=g)
+    tables = torch.zeros(spec["B"], width, dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(spec["lengths"]):
+        c = math.ceil(n / bs)
+        tables[b, :c] = perm[off:off + c].to(torch.int32)
+        off += c
+    q = torch.randn(spec["B"], spec["H"], spec["D"], generator=g).to(dtype)
+    k = torch.randn(blocks, bs, spec["KVH"], spec["D"], generator=g).to(dtype)
+    v = torch.randn(blocks, bs, spec["KVH"], spec["D"], generator=g).to(dtype)
+    return q, k, v, tables, lengths, max_len
+
+
+def rope_specs():
+    out = []
+    for dtype in ("float32", "float16"):
+        for D, theta in ((64, 1e5), (128, 5e5), (32, 1e4)):
+            out.append(dict(dtype=dtype, D=D, theta=theta, H=3, KVH=1, seed=77 + D))
+    return out
+
+
+ROPE_POSITIONS = [0, 1, 2, 15, 16, 17, 127, 128, 1000, 1023, 2047, 4095, 4096, 6000, 8190, 8191]
+
+
+def rope_inputs(spec):
+    dtype = getattr(torch, spec["dtype"])
+    g = torch.Generator().manual_seed(spec["seed"])
+    P = len(ROPE_POSITIONS)
+    q = (torch.randn(1, P, spec["H"], spec["D"], generator=g) * 3).to(dtype)
+    k = (torch.randn(1, P, spec["KVH"], spec["D"], generator=g) * 3).to(dtype)
+    pos = torch.tensor([ROPE_POSITIONS], dtype=torch.int64)
+    return q, k, pos
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    from worker.llama import PagedLlama, torch_paged_attention
+    from worker.engine import PagedKV
+
+    torch.set_num_threads(4)
+    fixtures = {}
+
+    # 1. The reference's own kernel test case (tests/test_llama.py:123-134), on CPU.
+    case = {}
+    for dtype in (torch.float32, torch.float16):
+        torch.manual_seed(11)
+        q = torch.randn(3, 4, 32, dtype=dtype)
+        keys = torch.randn(12, 16, 2, 32, dtype=dtype)
+        values = torch.randn_like(keys)
+        tables = torch.tensor([[9, 2, 5], [1, 8, 4], [7, 0, 6]], dtype=torch.int32)
+        lengths = torch.tensor([1, 17, 35], dtype=torch.int32)
+        out = torch_paged_attention(q, keys, values, tables, lengths, 35)
+        case[str(dtype).split(".")[1]] = dict(q=q, keys=keys, values=values, tables=tables,
+                                              lengths=lengths, max_length=35, out=out)
+    torch.save(case, HERE / "reference_kernel_case.pt")
+
+    # 2. Edge cases (outputs + input digests; inputs are regenerated from seeds).
+    edges = []
+    for spec in edge_case_specs():
+        q, k, v, tables, lengths, max_len = edge_case_inputs(spec)
+        out = torch_paged_attention(q, k, v, tables, lengths, max_len)
+        edges.append(dict(spec=spec, out=out, digests=[digest(t) for t in (q, k, v, tables, lengths)]))
+    torch.save(edges, HERE / "edge_cases.pt")
+
+    # 3. RoPE at page-boundary and large positions, both dtypes.
+    ropes = []
+    for spec in rope_specs():
+        q, k, pos = rope_inputs(spec)
+        inv = W.inv_freq(spec["theta"], spec["D"])
+        ref_inv = 1.0 / (spec["theta"] ** (torch.arange(0, spec["D"], 2, dtype=torch.float32) / spec["D"]))
+        assert torch.equal(inv, ref_inv)
+        qo, ko = PagedLlama.rope(_RopeHost(inv), q, k, pos)
+        ropes.append(dict(spec=spec, q=qo, k=ko, digests=[digest(q), digest(k)]))
+    torch.save(ropes, HERE / "rope_cases.pt")
+
+    # 4. Decode step of the SmolLM2 CPU workload: rope -> slot write -> attention.
+    w = W.smollm_cpu()
+    t = W.materialize(w, "cpu")
+    qn = t.q[0].unsqueeze(1)
+    kn = t.k[0].unsqueeze(1)
+    vn = t.v[0].unsqueeze(1)
+    qr, kr = PagedLlama.rope(_RopeHost(t.inv_freq), qn, kn, t.positions)
+    kp, vp = t.k_pools[0].clone(), t.v_pools[0].clone()
+    kp[t.physical, t.offsets] = kr[:, 0]
+    vp[t.physical, t.offsets] = vn[:, 0]
+    out = torch_paged_attention(qr[:, 0], kp, vp, t.tables, t.lengths, w.max_length)
+    fixtures_decode = dict(
+        lengths=w.lengths, tables=w.tables, q_roped=qr[:, 0], k_roped=kr[:, 0], out=out,
+        k_pool_digest=digest(kp), v_pool_digest=digest(vp),
+        input_digests=dict(q=digest(t.q[0]), k=digest(t.k[0]), v=digest(t.v[0]),
+                           k_pool=digest(t.k_pools[0]), v_pool=digest(t.v_pools[0])))
+    torch.save(fixtures_decode, HERE / "smollm_cpu_decode.pt")
+
+    # 5. Prefill RoPE + KV write (pool[slots] = k[valid]) of the prefill workload.
+    pw = W.prefill_smollm()
+    d = W.materialize_prefill(pw, "cpu")
+    qr, kr = PagedLlama.rope(_RopeHost(d["inv_freq"]), d["q"], d["k"], d["positions"])
+    kp, vp = d["k_pool"].clone(), d["v_pool"].clone()
+    kp[d["physical"], d["offsets"]] = kr[d["valid"]]
+    vp[d["physical"], d["offsets"]] = d["v"][d["valid"]]
+    torch.save(dict(q_roped_digest=digest(qr), k_roped_digest=digest(kr),
+                    k_pool_digest=digest(kp), v_pool_digest=digest(vp),
+                    input_digests=dict(q=digest(d["q"]), k=digest(d["k"]), v=digest(d["v"]),
+                                       k_pool=digest(d["k_pool"]), v_pool=digest(d["v_pool"]))),
+               HERE / "prefill.pt")
+
+    # 6. Dense-softmax known answer of the scalar spec (tests/test_engine.py:19-32).
+    kv = PagedKV(blocks=2, block_size=2)
+    kv.reserve("a", 3)
+    keys = [[1., 0.], [0., 1.], [1., 1.]]
+    vals = [[2., 0.], [0., 4.], [6., 8.]]
+    for kk, vv in zip(keys, vals):
+        kv.append("a", kk, vv)
+    fixtures["scalar"] = dict(q=[1., 2.], keys=keys, values=vals, block_size=2,
+                              table=kv.tables["a"], out=kv.attention("a", [1., 2.]))
+    torch.save(fixtures, HERE / "scalar_known_answer.pt")
+    print("wrote", sorted(p.name for p in HERE.glob("*.pt")))
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

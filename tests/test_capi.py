@@ -1,0 +1,144 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, validates arguments like cuda/binding.cpp:8-22, and the
+fast kernel's work partition covers every unit exactly once."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import REPO, import_module
+
+_lib = import_module("_lib")
+build = import_module("build")
+
+HEADER = REPO / "include" / "paged_decode_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build_library()
+    return _lib.load()
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pdb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_exports_every_declared_symbol(lib):
+    names = declared_symbols()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} lacks a ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.pdb_version()
+
+
+def attn(lib, **kw):
+    a = dict(B=2, H=4, D=32, N=12, bs=16, KVH=2, Dk=32, W=3, max_length=35, dtype=0)
+    a.update(kw)
+    return lib.pdb_paged_attention(None, None, None, None, None, None, a["B"], a["H"], a["D"],
+                                   a["N"], a["bs"], a["KVH"], a["Dk"], a["W"], a["max_length"],
+                                   a["dtype"], None, 0, None)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(B=0), "invalid query shape"),
+    (dict(D=257, Dk=257), "invalid query shape"),
+    (dict(H=0), "invalid query shape"),
+    (dict(N=0), "invalid cache shape"),
+    (dict(Dk=16), "invalid cache shape"),
+    (dict(KVH=3), "query heads must be a multiple of KV heads"),
+    (dict(dtype=7), "use FP32 or FP16"),
+    (dict(max_length=0), "invalid context bound"),
+    (dict(max_length=8193, W=600), "invalid context bound"),
+    (dict(max_length=49), "invalid context bound"),
+])
+def test_argument_checks_match_reference_messages(lib, kw, msg):
+    assert attn(lib, **kw) == 1
+    assert _lib.last_error() == msg
+
+
+def test_null_pointers_rejected_after_shape_checks(lib):
+    assert attn(lib) == 1
+    assert _lib.last_error() == "null tensor pointer"
+
+
+def test_rope_argument_checks(lib):
+    rc = lib.pdb_rope_kv_write(None, None, None, None, None, None, None, None, 0, 0, None, None,
+                               None, 2, None, 2, 1, 4, 2, 63, 8, 16, 1, None, 0, None)
+    assert rc == 1 and "even" in _lib.last_error()
+    rc = lib.pdb_rope_kv_write(None, None, None, None, None, None, None, None, 0, 0, None, None,
+                               None, 3, None, 2, 1, 4, 2, 64, 8, 16, 1, None, 0, None)
+    assert rc == 1 and "slots" in _lib.last_error()
+    assert lib.pdb_rope_kv_write_workspace_size(4, 100, 1) >= 400
+    assert lib.pdb_rope_kv_write_workspace_size(4, 100, 0) == 0
+
+
+def partition(lib, lengths, kvh, grid):
+    lens = np.asarray(lengths, dtype=np.int32)
+    ranges = np.zeros(2 * grid, dtype=np.int64)
+    total = lib.pdb_debug_partition(lens.ctypes.data, len(lens), kvh, grid, ranges.ctypes.data)
+    return total, ranges.reshape(grid, 2)
+
+
+@pytest.mark.parametrize("seed", range(5))
+def test_partition_covers_units_once_and_balances(lib, seed):
+    rng = np.random.default_rng(seed)
+    B = int(rng.integers(1, 300))
+    lengths = np.clip(np.round(rng.lognormal(np.log(1024), 0.8, B)), 0, 8192).astype(np.int32)
+    lengths[rng.random(B) < 0.1] = 0
+    kvh = int(rng.choice([1, 2, 3, 8]))
+    grid = int(rng.integers(1, 600))
+    total, r = partition(lib, lengths, kvh, grid)
+    assert total == kvh * int(np.sum((lengths.astype(np.int64) + 15) // 16))
+    assert r[0, 0] == 0 and r[-1, 1] == total
+    assert np.all(r[1:, 0] == r[:-1, 1])             # contiguous, no gap, no overlap
+    sizes = r[:, 1] - r[:, 0]
+    assert sizes.max() - sizes.min() <= 1            # equal shares of 16-token units
+
+
+def test_partition_owner_formula(lib):
+    """part_owner(u) (used by the combining CTA) is the CTA whose range holds u."""
+    lengths = [37, 0, 1000, 16, 17, 5000]
+    for grid in (1, 3, 7, 148, 592):
+        total, r = partition(lib, lengths, 8, grid)
+        for u in range(0, total, max(1, total // 97)):
+            owner = ((u + 1) * grid + total - 1) // total - 1
+            assert r[owner, 0] <= u < r[owner, 1]
+
+
+def test_workspace_size_without_device(lib):
+    # No GPU here: the fast-kernel part needs the device, the generic part does not.
+    n = lib.pdb_paged_attention_workspace_size(256, 32, 8, 128, 8192, 1)
+    assert n >= 256 * 32 * 16 * 130 * 4
+    assert lib.pdb_paged_attention_workspace_size(0, 32, 8, 128, 8192, 1) == 0
+
+
+def test_ops_reject_cpu_tensors(pkg):
+    q = torch.zeros(2, 4, 32)
+    k = torch.zeros(3, 16, 2, 32)
+    with pytest.raises(RuntimeError, match="query must be on CUDA"):
+        pkg.paged_attention(q, k, k, torch.zeros(2, 1, dtype=torch.int32),
+                            torch.zeros(2, dtype=torch.int32), 16)
+    with pytest.raises(RuntimeError, match="query must be on CUDA"):
+        pkg.rope_kv_write(q, k[0], k[0], k, k, torch.zeros(2, dtype=torch.long),
+                          torch.zeros(2, dtype=torch.long), torch.zeros(2, 1, dtype=torch.long),
+                          torch.zeros(16))
+
+
+def test_install_rebinds_module_global(pkg):
+    import types
+    mod = types.ModuleType("fake_llama")
+    mod.cuda_paged_attention = None
+    pkg.install(mod)
+    assert mod.cuda_paged_attention is pkg.cuda_paged_attention

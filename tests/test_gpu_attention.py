@@ -1,0 +1,163 @@
+"""GPU parity of paged_attention (both kernels) against the golden vectors and
+the CPU oracle, on the reference's own test case, its edge cases, the
+SmolLM2 and Llama-3-8B shaped workloads and random shapes."""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from conftest import REPO, golden_module, import_module
+from gpu_helpers import assert_parity, subset_pool
+from oracle import paged_attention as opa
+
+pytestmark = pytest.mark.gpu
+
+mg = golden_module()
+W = import_module("workloads")
+_lib = import_module("_lib")
+IMPLS = [_lib.IMPL_AUTO, _lib.IMPL_FAST, _lib.IMPL_GENERIC]
+
+
+def gold(name):
+    return torch.load(REPO / "tests" / "golden" / name, weights_only=False)
+
+
+def run(pkg, q, k, v, tables, lengths, max_length, impl, dev):
+    try:
+        out = pkg.paged_attention(q.to(dev), k.to(dev), v.to(dev), tables.to(dev),
+                                  lengths.to(dev), max_length, impl=impl)
+    except RuntimeError as e:
+        if impl == _lib.IMPL_FAST and "fast kernel does not support" in str(e):
+            pytest.skip("shape outside the fast kernel's instantiations")
+        raise
+    torch.cuda.synchronize()
+    return out.cpu()
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+@pytest.mark.parametrize("dtype", ["float32", "float16"])
+def test_reference_kernel_case(pkg, cuda, dtype, impl):
+    """tests/test_llama.py:123-134 of the reference: fragmented pages, lengths 1/17/35."""
+    c = gold("reference_kernel_case.pt")[dtype]
+    out = run(pkg, c["q"], c["keys"], c["values"], c["tables"], c["lengths"], c["max_length"],
+              impl, cuda)
+    assert_parity(out, c["out"], f"{dtype} impl={impl}")
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_edge_cases(pkg, cuda, impl):
+    ran = 0
+    for case in gold("edge_cases.pt"):
+        q, k, v, tables, lengths, max_len = mg.edge_case_inputs(case["spec"])
+        try:
+            out = pkg.paged_attention(q.to(cuda), k.to(cuda), v.to(cuda), tables.to(cuda),
+                                      lengths.to(cuda), max_len, impl=impl).cpu()
+        except RuntimeError as e:
+            if impl == _lib.IMPL_FAST and "fast kernel does not support" in str(e):
+                continue
+            raise
+        assert_parity(out, case["out"], case["spec"]["name"])
+        assert torch.all(out[lengths == 0] == 0)
+        ran += 1
+    assert ran >= 8
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+@pytest.mark.parametrize("dtype", ["float32", "float16"])
+def test_stale_pool_bytes_are_never_read(pkg, cuda, dtype, impl):
+    """Every pool slot outside [0, len) of its sequence is NaN: the result must
+    be bit-identical to the run on a clean pool (reads bounded by lengths)."""
+    spec = [s for s in mg.edge_case_specs() if s["dtype"] == dtype][4]  # 32/8 heads, D 128
+    q, k, v, tables, lengths, max_len = mg.edge_case_inputs(spec)
+    clean = run(pkg, q, k, v, tables, lengths, max_len, impl, cuda)
+    bs = k.shape[1]
+    live = torch.zeros(k.shape[0], bs, dtype=torch.bool)
+    for b, n in enumerate(lengths.tolist()):
+        for t in range(n):
+            live[tables[b, t // bs], t % bs] = True
+    kn, vn = k.clone(), v.clone()
+    kn[~live] = float("nan")
+    vn[~live] = float("nan")
+    poisoned = run(pkg, q, kn, vn, tables, lengths, max_len, impl, cuda)
+    assert torch.equal(clean, poisoned)
+
+
+@pytest.mark.parametrize("impl", [_lib.IMPL_FAST, _lib.IMPL_GENERIC])
+def test_repeated_calls_are_deterministic(pkg, cuda, impl):
+    w = W.llama3_8b(batch=24, layers=1)
+    t = W.materialize(w, cuda)
+    outs = [pkg.paged_attention(t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths,
+                                w.max_length, impl=impl) for _ in range(5)]
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+
+
+def test_smollm_fp16_layer(pkg, cuda):
+    """SmolLM2 FP16 workload (batch 64, len U[128, 2048]), one layer vs the oracle."""
+    w = W.smollm_fp16(layers=1)
+    t = W.materialize(w, cuda)
+    out = pkg.paged_attention(t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths,
+                              w.max_length)
+    ref = opa.paged_attention(t.q[0].cpu(), t.k_pools[0].cpu(), t.v_pools[0].cpu(),
+                              w.tables, w.lengths, w.max_length)
+    assert_parity(out, ref, "smollm fp16")
+
+
+def test_llama3_full_batch(pkg, cuda):
+    """Llama-3-8B shape at the full batch of 256, one layer: the two kernels
+    agree everywhere, and 12 sequences (shortest, longest, random) match the
+    CPU oracle."""
+    w = W.llama3_8b(layers=1)
+    t = W.materialize(w, cuda)
+    fast = pkg.paged_attention(t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths,
+                               w.max_length, impl=_lib.IMPL_FAST)
+    generic = pkg.paged_attention(t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths,
+                                  w.max_length, impl=_lib.IMPL_GENERIC)
+    assert_parity(fast, generic.cpu(), "fast vs generic")
+    order = torch.argsort(w.lengths)
+    pick = torch.cat([order[:3], order[-3:], torch.randperm(w.batch, generator=torch.Generator().manual_seed(0))[:6]])
+    pick = pick.unique()
+    tabs, (kp, vp) = subset_pool(w.tables[pick], w.lengths[pick], [t.k_pools[0], t.v_pools[0]],
+                                 w.block_size)
+    lens = w.lengths[pick]
+    ref = opa.paged_attention(t.q[0][pick.to(cuda)].cpu(), kp, vp, tabs, lens, int(lens.max()))
+    assert_parity(fast.cpu()[pick], ref, "llama3 subset")
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_random_shapes(pkg, cuda, seed):
+    g = torch.Generator().manual_seed(seed)
+    dtype = [torch.float32, torch.float16][seed % 2]
+    D = [32, 64, 128][seed % 3]
+    KVH = [1, 2, 4][(seed // 2) % 3]
+    G = [1, 2, 3, 4][seed % 4]
+    H = KVH * G
+    bs = [8, 16, 32][(seed // 3) % 3]
+    B = int(torch.randint(1, 40, (1,), generator=g))
+    lengths = torch.randint(0, 700, (B,), generator=g).to(torch.int32)
+    lengths[0] = max(int(lengths[0]), 1)
+    max_len = int(lengths.max())
+    need = ((lengths.to(torch.int64) + bs - 1) // bs)
+    N = int(need.sum()) + 3
+    perm = torch.randperm(N, generator=g)
+    width = math.ceil(max_len / bs)
+    tables = torch.zeros(B, width, dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(need.tolist()):
+        tables[b, :n] = perm[off:off + n].to(torch.int32)
+        off += n
+    q = torch.randn(B, H, D, generator=g).to(dtype)
+    k = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
+    v = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
+    ref = opa.paged_attention(q, k, v, tables, lengths, max_len)
+    for impl in IMPLS:
+        out = pkg.paged_attention(q.to(cuda), k.to(cuda), v.to(cuda), tables.to(cuda),
+                                  lengths.to(cuda), max_len, impl=impl).cpu()
+        assert_parity(out, ref, f"seed {seed} impl {impl}")
+
+
+def test_no_device_errors_raised(pkg, cuda):
+    assert pkg.read_device_errors() == 0

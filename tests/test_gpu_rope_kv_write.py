@@ -1,0 +1,142 @@
+"""GPU parity of rope_kv_write (fused RoPE + paged KV-slot write).
+
+Bars: rotated q/k within 2e-3 (FP16) / 1e-5 relative (FP32) of the
+reference; written slots hold exactly the kernel's rotated k and the input v;
+every other pool byte is unchanged (bit-exact)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import REPO, golden_module, import_module
+from gpu_helpers import assert_parity
+from oracle import kv_cache, paged_attention as opa, rope as orope
+
+pytestmark = pytest.mark.gpu
+
+mg = golden_module()
+W = import_module("workloads")
+
+
+def gold(name):
+    return torch.load(REPO / "tests" / "golden" / name, weights_only=False)
+
+
+def exact_fraction(a, b):
+    return (a.cpu() == b.cpu()).float().mean().item()
+
+
+def test_rope_golden_positions(pkg, cuda):
+    """Positions 0..8191 incl. page boundaries, both dtypes, three head dims."""
+    for case in gold("rope_cases.pt"):
+        spec = case["spec"]
+        q, k, pos = mg.rope_inputs(spec)
+        P = q.shape[1]
+        v = torch.zeros_like(k)
+        pool = torch.zeros(P, 1, k.shape[2], k.shape[3], dtype=q.dtype)
+        phys = torch.arange(P, dtype=torch.int64)
+        offs = torch.zeros(P, dtype=torch.int64)
+        inv = W.inv_freq(spec["theta"], spec["D"]).to(cuda)
+        qo, ko = pkg.rope_kv_write(q.to(cuda), k.to(cuda), v.to(cuda), pool.to(cuda),
+                                   pool.clone().to(cuda), phys.to(cuda), offs.to(cuda),
+                                   pos.to(cuda), inv)
+        assert_parity(qo, case["q"], f"rope q {spec}")
+        assert_parity(ko, case["k"], f"rope k {spec}")
+        if q.dtype == torch.float16:
+            assert exact_fraction(qo, case["q"]) > 0.999
+
+
+def test_smollm_cpu_decode_step_matches_golden(pkg, cuda):
+    """SmolLM2 FP32 decode step: rope_kv_write then paged_attention, against
+    the reference's outputs; untouched pool bytes bit-exact."""
+    g = gold("smollm_cpu_decode.pt")
+    w = W.smollm_cpu()
+    t = W.materialize(w, "cpu")
+    kp, vp = t.k_pools[0].to(cuda), t.v_pools[0].to(cuda)
+    qo, ko = pkg.rope_kv_write(t.q[0].to(cuda), t.k[0].to(cuda), t.v[0].to(cuda), kp, vp,
+                               t.physical.to(cuda), t.offsets.to(cuda), t.positions.to(cuda),
+                               t.inv_freq.to(cuda))
+    out = pkg.paged_attention(qo, kp, vp, t.tables.to(cuda), t.lengths.to(cuda), w.max_length)
+    assert_parity(qo, g["q_roped"], "q")
+    assert_parity(ko, g["k_roped"], "k")
+    assert_parity(out, g["out"], "attention")
+    # pool: written slots == kernel's k / input v, everything else untouched
+    exp_k, exp_v = t.k_pools[0].clone(), t.v_pools[0].clone()
+    kv_cache.write_decode(exp_k, t.physical, t.offsets, ko.cpu())
+    kv_cache.write_decode(exp_v, t.physical, t.offsets, t.v[0])
+    assert torch.equal(kp.cpu(), exp_k) and torch.equal(vp.cpu(), exp_v)
+
+
+@pytest.mark.parametrize("inplace", [False, True])
+def test_decode_prologue_fp16(pkg, cuda, inplace):
+    """SmolLM2 FP16 decode prologue (batch 64) against the oracle."""
+    w = W.smollm_fp16(layers=1)
+    t = W.materialize(w, cuda)
+    k_before, v_before = t.k_pools[0].cpu(), t.v_pools[0].cpu()
+    q_in, k_in, v_in = t.q[0].clone(), t.k[0].clone(), t.v[0].clone()
+    qr, kr = orope.rope(q_in.cpu().unsqueeze(1), k_in.cpu().unsqueeze(1), w.positions(),
+                        t.inv_freq.cpu())
+    qo, ko = pkg.rope_kv_write(t.q[0], t.k[0], t.v[0], t.k_pools[0], t.v_pools[0],
+                               t.physical, t.offsets, t.positions, t.inv_freq, inplace=inplace)
+    assert_parity(qo, qr[:, 0], "q")
+    assert_parity(ko, kr[:, 0], "k")
+    assert exact_fraction(qo, qr[:, 0]) > 0.999 and exact_fraction(ko, kr[:, 0]) > 0.999
+    if inplace:
+        assert qo.data_ptr() == t.q[0].data_ptr()
+    else:
+        assert torch.equal(t.q[0], q_in)
+    exp_k, exp_v = k_before.clone(), v_before.clone()
+    phys, off = w.slots()
+    kv_cache.write_decode(exp_k, phys, off, ko.cpu())
+    kv_cache.write_decode(exp_v, phys, off, v_in.cpu())
+    assert torch.equal(t.k_pools[0].cpu(), exp_k)
+    assert torch.equal(t.v_pools[0].cpu(), exp_v)
+
+
+def test_prefill_write(pkg, cuda):
+    """Prefill RoPE + KV write (16 prompts into a 4096-block pool): untouched
+    blocks byte-for-byte, written slots equal the rotated k / input v."""
+    g = gold("prefill.pt")
+    pw = W.prefill_smollm()
+    d = W.materialize_prefill(pw, "cpu")
+    qr, kr = orope.rope(d["q"], d["k"], d["positions"], d["inv_freq"])
+    dd = {k: v.to(cuda) for k, v in d.items()}
+    qo, ko = pkg.rope_kv_write(dd["q"], dd["k"], dd["v"], dd["k_pool"], dd["v_pool"],
+                               dd["physical"], dd["offsets"], dd["positions"], dd["inv_freq"],
+                               valid=dd["valid"])
+    assert_parity(qo, qr, "prefill q")
+    assert_parity(ko, kr, "prefill k")
+    exp_k, exp_v = d["k_pool"].clone(), d["v_pool"].clone()
+    kv_cache.write_prefill(exp_k, d["physical"], d["offsets"], ko.cpu(), d["valid"])
+    kv_cache.write_prefill(exp_v, d["physical"], d["offsets"], d["v"], d["valid"])
+    assert torch.equal(dd["k_pool"].cpu(), exp_k)
+    assert torch.equal(dd["v_pool"].cpu(), exp_v)
+    touched = torch.zeros(pw.num_blocks, dtype=torch.bool)
+    touched[d["physical"].unique()] = True
+    assert torch.equal(dd["k_pool"].cpu()[~touched], d["k_pool"][~touched])
+    # byte-identical to the reference whenever its cos/sin agree with ours
+    same = mg.digest(dd["k_pool"]) == g["k_pool_digest"]
+    print(f"prefill pool digest equal to the reference: {same}; "
+          f"k exact fraction {exact_fraction(ko, kr):.6f}")
+    assert pkg.read_device_errors() == 0
+
+
+def test_prologue_then_attention_llama3(pkg, cuda):
+    """Llama-3-8B shape, one layer, batch 256: prologue + attention on the GPU
+    against the oracle pipeline for 8 sequences."""
+    w = W.llama3_8b(layers=1)
+    t = W.materialize(w, cuda)
+    qo, ko = pkg.rope_kv_write(t.q[0], t.k[0], t.v[0], t.k_pools[0], t.v_pools[0],
+                               t.physical, t.offsets, t.positions, t.inv_freq)
+    out = pkg.paged_attention(qo, t.k_pools[0], t.v_pools[0], t.tables, t.lengths, w.max_length)
+    qr, kr = orope.rope(t.q[0].cpu().unsqueeze(1), t.k[0].cpu().unsqueeze(1), w.positions(),
+                        t.inv_freq.cpu())
+    assert_parity(qo, qr[:, 0], "q")
+    assert_parity(ko, kr[:, 0], "k")
+    from gpu_helpers import subset_pool
+    pick = torch.argsort(w.lengths)[torch.tensor([0, 1, 64, 128, 200, 253, 254, 255])]
+    tabs, (kp, vp) = subset_pool(w.tables[pick], w.lengths[pick], [t.k_pools[0], t.v_pools[0]],
+                                 w.block_size)
+    lens = w.lengths[pick]
+    ref = opa.paged_attention(qo.cpu()[pick], kp, vp, tabs, lens, int(lens.max()))
+    assert_parity(out.cpu()[pick], ref, "llama3 pipeline")
