@@ -79,13 +79,27 @@ class ClockSampler:
         try:
             import pynvml
             pynvml.nvmlInit()
-            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
             self._nvml = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode() if isinstance(bus, str) else bus)
+            self._h = self._handle(pynvml, torch.cuda.get_device_properties(device_index))
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
         except Exception as e:  # noqa: BLE001 - report, never fail the bench
             self.error = f"nvml unavailable: {e}"
             self._nvml = None
+
+    @staticmethod
+    def _handle(nv, props):
+        """NVML handle of the CUDA device: match by UUID, else by the PCI
+        address string built from torch's integer domain/bus/device ids."""
+        want = str(props.uuid).lower().removeprefix("gpu-")
+        for i in range(nv.nvmlDeviceGetCount()):
+            h = nv.nvmlDeviceGetHandleByIndex(i)
+            uid = nv.nvmlDeviceGetUUID(h)
+            uid = (uid.decode() if isinstance(uid, bytes) else str(uid)).lower().removeprefix("gpu-")
+            if uid == want:
+                return h
+        addr = "%08X:%02X:%02X.0" % (int(props.pci_domain_id), int(props.pci_bus_id),
+                                     int(props.pci_device_id))
+        return nv.nvmlDeviceGetHandleByPciBusId(addr.encode())
 
     def _run(self):
         nv = self._nvml
@@ -258,7 +272,7 @@ def e2e_run(w, t, steps, warmup, device):
     return ms, h2d_bytes, d2h_bytes, check
 
 
-def cpu_baseline(w, t, budget_s=20.0, sample=32):
+def cpu_baseline(w, t, budget_s=15.0, sample=16):
     """The reference's CPU path (oracle port of worker/llama.py:108-117,
     :171-172, :58-71) on `sample` sequences of layer 0, all host threads,
     padded to the batch max_length like the reference; scaled to seq-steps/s
@@ -285,7 +299,7 @@ def cpu_baseline(w, t, budget_s=20.0, sample=32):
         kv_cache.write_decode(vp, phys, off, v)
         opa.paged_attention(qr[:, 0], kp, vp, tabs, lens, w.max_length)
         times.append(time.perf_counter() - t0)
-        if len(times) >= 5:
+        if len(times) >= 3:
             break
     per_layer = statistics.median(times)
     return {"value": len(idx) / (per_layer * w.layers), "unit": UNIT,
@@ -420,14 +434,14 @@ def run_reference(args):
     """The reference's own CPU implementation of the path (oracle port of
     worker/llama.py:58-71, :108-117, :171-172; the reference compiles no
     CPU code) on the host cores, same workload/metric. Each step is a
-    bounded sample: 8 sequences of one layer, scaled to seq-steps/s."""
+    bounded sample: 4 sequences of one layer, scaled to seq-steps/s."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
     from oracle import kv_cache, paged_attention as opa, rope as orope
     torch.set_num_threads(os.cpu_count() or 1)
     full = make_workload(args)
-    n = min(8, full.batch)
+    n = min(4, full.batch)
     tabs, blocks, used = W.make_decode_tables(full.lengths[:n], full.block_size, full.seed, 1.25, None)
     # pad the sample's tables to the batch's width, as TensorPagedKV.metadata does
     wide = torch.zeros(n, full.table_width, dtype=torch.int32)

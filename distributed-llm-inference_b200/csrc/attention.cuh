@@ -204,7 +204,6 @@ attn_fast_kernel(const AttnParams p) {
   if (tid == 0) P[B] = misc[0];
   __syncthreads();
   const int64_t U = P[B];
-  const int64_t grid = gridDim.x;
 
   // zero-length sequences produce zeros (cuda/paged_attention.cu:56)
   for (int b = blockIdx.x; b < B; b += gridDim.x) {
@@ -214,6 +213,10 @@ attn_fast_kernel(const AttnParams p) {
     }
   }
 
+  // Effective grid: never more CTAs than units, so every working CTA owns at
+  // least one unit and the CTAs covering a segment are exactly its pieces.
+  const int64_t grid = part_grid(gridDim.x, U);
+  if ((int64_t)blockIdx.x >= grid) return;
   const int64_t u_beg = part_begin(blockIdx.x, U, grid);
   const int64_t u_end = part_begin(blockIdx.x + 1, U, grid);
   if (u_beg >= u_end) return;

@@ -99,9 +99,15 @@ __device__ __forceinline__ void cp_async_wait() {
 // ---- work partition shared by host and device --------------------------------
 // The fast kernel flattens the work of one call into "units" of 16 tokens,
 // ordered by (sequence, kv_head, token). Sequence b contributes
-// kv_heads * ceil(len_b / 16) units. CTA c owns units [begin(c), begin(c+1)).
+// kv_heads * ceil(len_b / 16) units. CTA c < part_grid owns units
+// [begin(c), begin(c+1)); CTAs beyond part_grid own nothing.
 constexpr int kUnitTokens = 16;
 
+// CTAs that take part: min(launched, total units), so that with
+// begin(c) = c*total/grid every participating CTA owns at least one unit.
+__host__ __device__ __forceinline__ int64_t part_grid(int64_t launched, int64_t total) {
+  return launched < total ? launched : total;
+}
 __host__ __device__ __forceinline__ int64_t part_begin(int64_t c, int64_t total,
                                                        int64_t grid) {
   return (c * total) / grid;

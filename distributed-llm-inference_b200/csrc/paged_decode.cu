@@ -401,9 +401,10 @@ int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch, int64_t kv_he
     const int64_t len = lengths[b] < 0 ? 0 : lengths[b];
     U += kv_heads * ((len + pdb::kUnitTokens - 1) / pdb::kUnitTokens);
   }
+  const int64_t g = pdb::part_grid(grid, U);
   for (int64_t c = 0; c < grid; ++c) {
-    ranges[2 * c] = pdb::part_begin(c, U, grid);
-    ranges[2 * c + 1] = pdb::part_begin(c + 1, U, grid);
+    ranges[2 * c] = c < g ? pdb::part_begin(c, U, g) : U;
+    ranges[2 * c + 1] = c < g ? pdb::part_begin(c + 1, U, g) : U;
   }
   return U;
 }

@@ -28,6 +28,8 @@ from dataclasses import dataclass, field
 
 import torch
 
+from .sharding import shard_bounds
+
 
 @dataclass
 class DecodeWorkload:
@@ -105,7 +107,7 @@ class DecodeWorkload:
         Each rank owns its KV pool and block tables; the shard's tables are
         renumbered into a pool of the shard's own size.
         """
-        lo, hi = rank * self.batch // world, (rank + 1) * self.batch // world
+        lo, hi = shard_bounds(self.batch, world, rank)
         lengths = self.lengths[lo:hi].clone()
         sub = make_decode_tables(lengths, self.block_size, self.seed * 1000 + rank,
                                  self.meta.get("pool_factor", 1.25), None)
