@@ -44,19 +44,26 @@ int sm_count(int dev) {
   return n;
 }
 
-// Occupancy (CTAs per SM) of `fn` with `smem` dynamic bytes on `dev`; also
-// raises the function's dynamic shared-memory limit on first use.
+// Occupancy (CTAs per SM) of `fn` with `smem` dynamic bytes on `dev`. The
+// function's dynamic shared-memory limit is only ever raised (per device and
+// function), so a launch with a smaller request never lowers the limit that
+// an earlier, larger configuration relies on.
 int ctas_per_sm(int dev, const void* fn, size_t smem, int threads) {
   static std::map<std::tuple<int, const void*, size_t>, int> cache;
+  static std::map<std::pair<int, const void*>, size_t> limit;
   std::lock_guard<std::mutex> lk(g_mu);
   auto key = std::make_tuple(dev, fn, smem);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess) {
-    cudaGetLastError();
-    cache[key] = 0;
-    return 0;
+  size_t& cur = limit[std::make_pair(dev, fn)];
+  if (smem > cur) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      cache[key] = 0;
+      return 0;
+    }
+    cur = smem;
   }
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem) != cudaSuccess) {
