@@ -7,8 +7,19 @@
 // cuda/paged_attention.cu:10-58 and of torch_paged_attention in
 // worker/llama.py:58-71.
 //
-// Two kernels:
-//  * attn_fast_kernel — persistent, one work list per call.
+// Kernels:
+//  * attn_streamk_kernel<Math> — persistent stream-K decode, one launch per
+//    call, with two inner loops ("Math" policies):
+//      - MmaMath  (FP16, head_dim 64/128, group <= 8): tensor cores.
+//        S^T = K Q^T with mma.sync.m16n8k16 (16 tokens x 8 query heads per
+//        warp, fp32 accumulate), online softmax in fp32, P^T moved into the
+//        B operand with movmatrix, O^T += V^T P^T with P split into two FP16
+//        terms (hi + lo) so the weights keep ~22 bits. K/V tiles are staged by
+//        cp.async into an XOR-swizzled layout that ldmatrix reads without
+//        bank conflicts.
+//      - SimtMath (FP32 and the remaining FP16 shapes): fp32 FMA; lanes split
+//        a token row into 16-byte chunks, warp-shuffle reductions.
+//    Shared by both:
 //      - Work is flattened into 16-token units ordered by (sequence, kv head,
 //        token). CTA c owns the contiguous unit range [c*U/grid, (c+1)*U/grid),
 //        so every CTA streams the same number of K/V bytes whatever the
@@ -16,10 +27,6 @@
 //      - A CTA stages each K/V tile of one kv head into shared memory once
 //        (cp.async, STAGES-deep ring) and all G query heads of the GQA group
 //        read it there: K/V cross HBM exactly once.
-//      - QK: lanes of a warp split a token row into 16-byte chunks
-//        (conflict-free LDS.128), q lives in registers, scores are reduced
-//        with warp shuffles. Online softmax in fp32 (base 2). PV: each lane
-//        owns D/32 output dims; probabilities are broadcast through smem.
 //      - A (sequence, kv head) segment cut by a CTA boundary is a "piece":
 //        its partial (m, l, o) goes to the workspace and the last CTA to
 //        finish a piece of that segment (epoch-tagged arrival counter, no
@@ -50,8 +57,8 @@ struct AttnParams {
   int max_length;
   float scale_log2;  // log2(e) / sqrt(D)
   // workspace
-  unsigned long long* counters;  // fast: [B*KVH] epoch<<32 | arrivals
-  float* partials;               // fast: [2*grid][GP*(D+2)]; generic: [B*H*splits][D+2]
+  unsigned long long* counters;  // stream-K: [B*KVH] epoch<<32 | arrivals
+  float* partials;               // stream-K: [2*grid][GP*(D+2)]; generic: [B*H*splits][D+2]
   uint32_t epoch;
   int splits;  // generic
   int chunk;   // generic: tokens per split
@@ -68,46 +75,53 @@ __device__ __forceinline__ int checked_length(const int32_t* lengths, int b,
   return len;
 }
 
-// ===========================================================================
-// Fast kernel
-// ===========================================================================
-template <typename T, int D_, int GP_, int TPG_, int STAGES_>
-struct FastTraits {
-  using Elem_t = T;
-  static constexpr int D = D_;
-  static constexpr int GP = GP_;          // group size padded to a power of 2
-  static constexpr int TPG = TPG_;        // tokens per lane group per tile
-  static constexpr int STAGES = STAGES_;  // cp.async ring depth
-  static constexpr int E = sizeof(T);
-  static constexpr int VEC = 16 / E;  // elements per 16-byte chunk
-  static constexpr int CH = D / VEC;  // chunks per token row
-  static constexpr int LPT = CH < 8 ? CH : 8;  // lanes per token (QK)
-  static constexpr int CPL = CH / LPT;         // chunks per lane (QK)
-  static constexpr int DL = CPL * VEC;         // dims per lane (QK)
-  static constexpr int TPW = 32 / LPT;         // lane groups per warp
-  static constexpr int NW = 4;
-  static constexpr int NT = NW * 32;
-  static constexpr int TW = TPW * TPG;      // tokens per warp per tile
-  static constexpr int TILE = NW * TW;      // tokens per tile
-  static constexpr int TILE_UNITS = TILE / kUnitTokens;
-  static constexpr int DPL = D / 32;        // dims per lane (PV)
-  static constexpr int ROW = D * E;         // bytes per token row
-  static constexpr int TILE_BYTES = TILE * ROW;
-  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  static constexpr int PS_FLOATS = NW * TW * GP;
-  static constexpr int MERGE_FLOATS = NW * GP * (D + 2);
-  static constexpr int SLOT_FLOATS = GP * (D + 2);
-  static_assert(TILE % kUnitTokens == 0, "tile must hold whole units");
-  static_assert(D % 32 == 0 && CH % LPT == 0, "unsupported head_dim");
-  static_assert(DPL * E <= 16, "PV lane width");
+// ---- tensor-core and shared-memory primitives --------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                        const void* p) {
+  const unsigned a = static_cast<unsigned>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                          const void* p) {
+  const unsigned a = static_cast<unsigned>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a)
+               : "memory");
+}
+// D += A(16x16, row) * B(16x8, col), fp16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Transpose an 8x8 fp16 matrix held as the standard m8n8 warp fragment.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 
-  static size_t smem_bytes(int B) {
-    return (size_t)STAGES * STAGE_BYTES + (size_t)(PS_FLOATS + MERGE_FLOATS) * 4 +
-           (size_t)(2 * B + 1 + 8) * 4;
-  }
-};
+// Byte offset of 16-byte chunk `col` of token row `row` in a staged tile.
+// SWZ: chunk positions are XOR-ed with (row & 7), so the 8 rows that one
+// ldmatrix 8x8 load touches fall into 8 different bank groups.
+template <int ROW_BYTES, bool SWZ>
+__device__ __forceinline__ int tile_offset(int row, int col) {
+  return row * ROW_BYTES + ((SWZ ? (col ^ (row & 7)) : col) << 4);
+}
 
-// Position in the flattened unit stream of one CTA.
+// ===========================================================================
+// Work partition (identical in every CTA, recomputed from device lengths)
+// ===========================================================================
 struct Cursor {
   int b, h, nu;     // sequence, kv head, units per kv head of sequence b
   int64_t seg;      // first unit of segment (b, h)
@@ -152,39 +166,28 @@ __device__ __forceinline__ void cursor_advance(Cursor& c, int64_t te, int64_t u_
   }
 }
 
-template <class Tr>
-__global__ void __launch_bounds__(Tr::NT)
-attn_fast_kernel(const AttnParams p) {
-  using T = typename Tr::Elem_t;
-  constexpr int D = Tr::D, GP = Tr::GP, TPG = Tr::TPG, STAGES = Tr::STAGES;
-  constexpr int VEC = Tr::VEC, CH = Tr::CH, LPT = Tr::LPT, CPL = Tr::CPL;
-  constexpr int DL = Tr::DL, TPW = Tr::TPW, NW = Tr::NW, NT = Tr::NT;
-  constexpr int TW = Tr::TW, TILE = Tr::TILE, DPL = Tr::DPL;
+// Valid tokens of the tile [c.u, te) of segment c.
+__device__ __forceinline__ int tile_tokens(const Cursor& c, int64_t te, const int* Ls) {
+  const int tok0 = (int)(c.u - c.seg) * kUnitTokens;
+  const int rem = Ls[c.b] - tok0;
+  const int span = (int)(te - c.u) * kUnitTokens;
+  return span < rem ? span : rem;
+}
 
-  extern __shared__ __align__(128) unsigned char smem[];
-  float* ps = reinterpret_cast<float*>(smem + (size_t)STAGES * Tr::STAGE_BYTES);
-  float* ms = ps + Tr::PS_FLOATS;  // [NW][GP]
-  float* ls = ms + NW * GP;        // [NW][GP]
-  float* accs = ls + NW * GP;      // [NW][GP][D]
-  int* P = reinterpret_cast<int*>(accs + NW * GP * D);  // [B+1]
-  int* Ls = P + p.B + 1;                                 // [B]
-  int* misc = Ls + p.B;                                  // [8]
-
+// P[b] = KVH * sum_{b' < b} ceil(len_b' / 16) and the clamped lengths Ls.
+// Returns the total unit count U. All threads of the CTA call it.
+template <int NT>
+__device__ int64_t plan_units(const AttnParams& p, int* P, int* Ls, int* misc) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int B = p.B, KVH = p.KVH;
-  const T* __restrict__ kpool = static_cast<const T*>(p.k_pool);
-  const T* __restrict__ vpool = static_cast<const T*>(p.v_pool);
-
-  // ---- plan: P[b] = KVH * sum_{b' < b} ceil(len_b' / 16) -------------------
   if (tid == 0) misc[0] = 0;
   __syncthreads();
-  for (int base = 0; base < B; base += NT) {
+  for (int base = 0; base < p.B; base += NT) {
     const int b = base + tid;
     int nu = 0;
-    if (b < B) {
+    if (b < p.B) {
       const int len = checked_length(p.lengths, b, p.max_length);
       Ls[b] = len;
-      nu = ((len + kUnitTokens - 1) / kUnitTokens) * KVH;
+      nu = ((len + kUnitTokens - 1) / kUnitTokens) * p.KVH;
     }
     int incl = nu;
 #pragma unroll
@@ -196,17 +199,412 @@ attn_fast_kernel(const AttnParams p) {
     __syncthreads();
     int woff = misc[0];
     for (int w = 0; w < warp; ++w) woff += misc[4 + w];
-    if (b < B) P[b] = woff + incl - nu;
+    if (b < p.B) P[b] = woff + incl - nu;
     __syncthreads();
     if (tid == NT - 1) misc[0] = woff + incl;
     __syncthreads();
   }
-  if (tid == 0) P[B] = misc[0];
+  if (tid == 0) P[p.B] = misc[0];
   __syncthreads();
-  const int64_t U = P[B];
+  return P[p.B];
+}
+
+// Stage the K and V rows of tile [c.u, te) into shared memory (cp.async,
+// zero-fill beyond the valid tokens). Table entries are range-checked before
+// any address is formed; a bad entry raises PDB_DEVERR_TABLE_ENTRY and its
+// rows are zero-filled.
+template <typename T, int D, int TILE, int NT, bool SWZ>
+__device__ __forceinline__ void load_tile(const AttnParams& p, const int* Ls, const Cursor& c,
+                                          int64_t te, unsigned char* sk, unsigned char* sv) {
+  constexpr int VEC = 16 / (int)sizeof(T), CH = D / VEC, ROW = D * (int)sizeof(T);
+  static_assert(NT % CH == 0, "rows per pass");
+  constexpr int RPP = NT / CH;  // rows per pass
+  const T* kpool = static_cast<const T*>(p.k_pool);
+  const T* vpool = static_cast<const T*>(p.v_pool);
+  const int tok0 = (int)(c.u - c.seg) * kUnitTokens;
+  const int ntok = tile_tokens(c, te, Ls);
+  const int32_t* trow = p.tables + (int64_t)c.b * p.table_width;
+  const int col = threadIdx.x % CH;
+  int last_pi = -1, page = 0;
+#pragma unroll
+  for (int k = 0; k < TILE / RPP; ++k) {
+    const int row = threadIdx.x / CH + k * RPP;
+    bool ok = row < ntok;
+    const T* ks = kpool;
+    const T* vs = vpool;
+    if (ok) {
+      const int t = tok0 + row;
+      int pi, off;
+      if (p.bs_shift >= 0) {
+        pi = t >> p.bs_shift;
+        off = t & (p.block_size - 1);
+      } else {
+        pi = t / p.block_size;
+        off = t - pi * p.block_size;
+      }
+      if (pi != last_pi) {
+        page = __ldg(trow + pi);
+        last_pi = pi;
+      }
+      if (page < 0 || (int64_t)page >= p.num_blocks) {
+        raise_error(0x1u);
+        ok = false;
+      } else {
+        const int64_t e = (((int64_t)page * p.block_size + off) * p.KVH + c.h) * D + col * VEC;
+        ks = kpool + e;
+        vs = vpool + e;
+      }
+    }
+    const int o = tile_offset<ROW, SWZ>(row, col);
+    cp_async16(sk + o, ks, ok);
+    cp_async16(sv + o, vs, ok);
+  }
+}
+
+// ===========================================================================
+// Inner loop 1: tensor cores (FP16)
+// ===========================================================================
+// GQ: query heads of the group that are kept (4 or 8); the MMA N dimension
+// always computes 8 columns, columns >= G see q = 0 and are never stored.
+template <int D_, int GQ_, int STAGES_>
+struct MmaMath {
+  using T = __half;
+  static constexpr int D = D_, GP = GQ_, STAGES = STAGES_;
+  static constexpr int NW = 4, NT = 128;
+  static constexpr int WT = 16;          // tokens per warp per tile (MMA M)
+  static constexpr int TILE = NW * WT;   // 64 tokens
+  static constexpr int TILE_UNITS = TILE / kUnitTokens;
+  static constexpr bool SWZ = true;
+  static constexpr int KSTEPS = D / 16;  // QK k-steps == PV m-tiles
+  static constexpr int ROW = D * 2;
+  static constexpr int TILE_BYTES = TILE * ROW;
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  static constexpr int EXTRA_FLOATS = 0;
+  static_assert(D % 64 == 0, "swizzle needs >= 8 chunks per row");
+  static_assert(GQ_ == 4 || GQ_ == 8, "group");
+
+  struct State {
+    uint32_t qb[KSTEPS][2];  // B fragments of Q^T (8 heads)
+    float m[2], l[2];        // heads 2*tg, 2*tg+1
+    float acc[KSTEPS][4];    // O^T fragments: dims x heads
+  };
+
+  __device__ static void begin_piece(State& s, const AttnParams& p, int b, int h) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    const bool real = g < p.G;  // columns >= G are padding (q = 0)
+    const __half* qrow = static_cast<const __half*>(p.q) +
+                         ((int64_t)b * p.H + (int64_t)h * p.G + (real ? g : 0)) * D;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+      s.qb[ks][0] = real ? __ldg(reinterpret_cast<const unsigned*>(qrow + 16 * ks + 2 * tg)) : 0u;
+      s.qb[ks][1] = real ? __ldg(reinterpret_cast<const unsigned*>(qrow + 16 * ks + 2 * tg + 8)) : 0u;
+    }
+    s.m[0] = s.m[1] = -INFINITY;
+    s.l[0] = s.l[1] = 0.f;
+#pragma unroll
+    for (int i = 0; i < KSTEPS; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s.acc[i][j] = 0.f;
+  }
+
+  __device__ static void compute_tile(State& s, const AttnParams& p, const unsigned char* sk,
+                                      const unsigned char* sv, int ntok, float*) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = warp * WT;
+    if (r0 >= ntok) return;  // warp-uniform: no valid token in this warp's rows
+    const int g = lane >> 2, mi = lane >> 3;
+
+    // S^T[16 tokens x 8 heads] = K[16 x D] . Q^T[D x 8]; two chains for ILP
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int row = r0 + ((mi & 1) << 3) + (lane & 7);
+#pragma unroll
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(a0, a1, a2, a3, sk + tile_offset<ROW, true>(row, 2 * ks + (mi >> 1)));
+        mma_16816((ks & 1) ? c1 : c0, a0, a1, a2, a3, s.qb[ks][0], s.qb[ks][1]);
+      }
+    }
+    const bool v0 = r0 + g < ntok, v1 = r0 + g + 8 < ntok;
+    const float sc = p.scale_log2;
+    const float sA0 = v0 ? (c0[0] + c1[0]) * sc : -INFINITY;  // token g,   head 2tg
+    const float sB0 = v0 ? (c0[1] + c1[1]) * sc : -INFINITY;  // token g,   head 2tg+1
+    const float sA1 = v1 ? (c0[2] + c1[2]) * sc : -INFINITY;  // token g+8, head 2tg
+    const float sB1 = v1 ? (c0[3] + c1[3]) * sc : -INFINITY;  // token g+8, head 2tg+1
+
+    float mA = fmaxf(sA0, sA1), mB = fmaxf(sB0, sB1);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mA = fmaxf(mA, __shfl_xor_sync(0xffffffffu, mA, o));
+      mB = fmaxf(mB, __shfl_xor_sync(0xffffffffu, mB, o));
+    }
+    const float nA = fmaxf(s.m[0], mA), nB = fmaxf(s.m[1], mB);
+    const bool grow = (nA > s.m[0]) || (nB > s.m[1]);
+    if (__any_sync(0xffffffffu, grow)) {
+      const float aA = (s.m[0] == -INFINITY) ? 0.f : exp2f(s.m[0] - nA);
+      const float aB = (s.m[1] == -INFINITY) ? 0.f : exp2f(s.m[1] - nB);
+      s.l[0] *= aA;
+      s.l[1] *= aB;
+#pragma unroll
+      for (int i = 0; i < KSTEPS; ++i) {
+        s.acc[i][0] *= aA; s.acc[i][1] *= aB;
+        s.acc[i][2] *= aA; s.acc[i][3] *= aB;
+      }
+      s.m[0] = nA;
+      s.m[1] = nB;
+    }
+    const float pA0 = (sA0 == -INFINITY) ? 0.f : exp2f(sA0 - s.m[0]);
+    const float pB0 = (sB0 == -INFINITY) ? 0.f : exp2f(sB0 - s.m[1]);
+    const float pA1 = (sA1 == -INFINITY) ? 0.f : exp2f(sA1 - s.m[0]);
+    const float pB1 = (sB1 == -INFINITY) ? 0.f : exp2f(sB1 - s.m[1]);
+    s.l[0] += pA0 + pA1;
+    s.l[1] += pB0 + pB1;
+
+    // P^T as two FP16 B operands (hi + lo): the transposes of the C fragment.
+    const uint32_t h0 = pack_half2(pA0, pB0), h1 = pack_half2(pA1, pB1);
+    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
+    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&h1));
+    const uint32_t l0 = pack_half2(pA0 - f0.x, pB0 - f0.y), l1 = pack_half2(pA1 - f1.x, pB1 - f1.y);
+    const uint32_t bh0 = movmatrix_t(h0), bh1 = movmatrix_t(h1);
+    const uint32_t bl0 = movmatrix_t(l0), bl1 = movmatrix_t(l1);
+
+    // O^T[D x 8] += V^T[D x 16 tokens] . P^T[16 x 8]
+    const int vrow = r0 + ((mi >> 1) << 3) + (lane & 7);
+#pragma unroll
+    for (int md = 0; md < KSTEPS; ++md) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(a0, a1, a2, a3, sv + tile_offset<ROW, true>(vrow, 2 * md + (mi & 1)));
+      mma_16816(s.acc[md], a0, a1, a2, a3, bh0, bh1);
+      mma_16816(s.acc[md], a0, a1, a2, a3, bl0, bl1);
+    }
+  }
+
+  // Publish this warp's (m, l, O) for the heads < GQ into the merge area.
+  __device__ static void store_state(State& s, float* ms, float* ls, float* accs) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      s.l[0] += __shfl_xor_sync(0xffffffffu, s.l[0], o);
+      s.l[1] += __shfl_xor_sync(0xffffffffu, s.l[1], o);
+    }
+    const int hA = 2 * tg, hB = 2 * tg + 1;
+    if (hB < GP) {
+      if (g == 0) {
+        ms[warp * GP + hA] = s.m[0]; ms[warp * GP + hB] = s.m[1];
+        ls[warp * GP + hA] = s.l[0]; ls[warp * GP + hB] = s.l[1];
+      }
+      float* oa = accs + (warp * GP + hA) * D;
+      float* ob = accs + (warp * GP + hB) * D;
+#pragma unroll
+      for (int md = 0; md < KSTEPS; ++md) {
+        oa[16 * md + g] = s.acc[md][0];
+        ob[16 * md + g] = s.acc[md][1];
+        oa[16 * md + g + 8] = s.acc[md][2];
+        ob[16 * md + g + 8] = s.acc[md][3];
+      }
+    }
+  }
+};
+
+// ===========================================================================
+// Inner loop 2: SIMT fp32 FMA (FP32, and FP16 shapes outside MmaMath)
+// ===========================================================================
+template <typename T_, int D_, int GP_, int TPG_, int STAGES_>
+struct SimtMath {
+  using T = T_;
+  static constexpr int D = D_;
+  static constexpr int GP = GP_;          // group size padded to a power of 2
+  static constexpr int TPG = TPG_;        // tokens per lane group per tile
+  static constexpr int STAGES = STAGES_;  // cp.async ring depth
+  static constexpr int E = sizeof(T);
+  static constexpr int VEC = 16 / E;  // elements per 16-byte chunk
+  static constexpr int CH = D / VEC;  // chunks per token row
+  static constexpr int LPT = CH < 8 ? CH : 8;  // lanes per token (QK)
+  static constexpr int CPL = CH / LPT;         // chunks per lane (QK)
+  static constexpr int DL = CPL * VEC;         // dims per lane (QK)
+  static constexpr int TPW = 32 / LPT;         // lane groups per warp
+  static constexpr int NW = 4, NT = 128;
+  static constexpr int TW = TPW * TPG;      // tokens per warp per tile
+  static constexpr int TILE = NW * TW;      // tokens per tile
+  static constexpr int TILE_UNITS = TILE / kUnitTokens;
+  static constexpr int DPL = D / 32;        // dims per lane (PV)
+  static constexpr bool SWZ = false;
+  static constexpr int ROW = D * E;
+  static constexpr int TILE_BYTES = TILE * ROW;
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  static constexpr int EXTRA_FLOATS = NW * TW * GP;  // probability broadcast
+  static_assert(TILE % kUnitTokens == 0, "tile must hold whole units");
+  static_assert(D % 32 == 0 && CH % LPT == 0, "unsupported head_dim");
+  static_assert(DPL * E <= 16, "PV lane width");
+
+  struct State {
+    float q[GP][DL];
+    float m[GP], l[GP], acc[GP][DPL];
+  };
+
+  __device__ static void begin_piece(State& s, const AttnParams& p, int b, int h) {
+    const int l8 = (threadIdx.x & 31) % LPT;
+    const T* qb = static_cast<const T*>(p.q) + ((int64_t)b * p.H + (int64_t)h * p.G) * D;
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        if (g < p.G) {
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qb + g * D + (l8 + LPT * c) * VEC));
+          Chunk<T>::to_f(raw, &s.q[g][c * VEC]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) s.q[g][c * VEC + e] = 0.f;
+        }
+      }
+      s.m[g] = -INFINITY;
+      s.l[g] = 0.f;
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) s.acc[g][d] = 0.f;
+    }
+  }
+
+  __device__ static void compute_tile(State& st, const AttnParams& p, const unsigned char* skb,
+                                      const unsigned char* svb, int ntok, float* ps) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = lane / LPT, l8 = lane % LPT;
+    const T* sk = reinterpret_cast<const T*>(skb);
+    const T* sv = reinterpret_cast<const T*>(svb);
+    float s[GP][TPG];
+#pragma unroll
+    for (int r = 0; r < TPG; ++r) {
+      const int row = warp * TW + r * TPW + grp;
+      float part[GP];
+#pragma unroll
+      for (int g = 0; g < GP; ++g) part[g] = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        float kf[VEC];
+        lds_to_f<T, VEC>(sk + row * D + (l8 + LPT * c) * VEC, kf);
+#pragma unroll
+        for (int g = 0; g < GP; ++g)
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) part[g] = fmaf(st.q[g][c * VEC + e], kf[e], part[g]);
+      }
+#pragma unroll
+      for (int o = 1; o < LPT; o <<= 1)
+#pragma unroll
+        for (int g = 0; g < GP; ++g) part[g] += __shfl_xor_sync(0xffffffffu, part[g], o);
+#pragma unroll
+      for (int g = 0; g < GP; ++g) s[g][r] = row < ntok ? part[g] * p.scale_log2 : -INFINITY;
+    }
+
+    // tile max, lazy rescale (m is warp-uniform)
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+      float mt = s[g][0];
+#pragma unroll
+      for (int r = 1; r < TPG; ++r) mt = fmaxf(mt, s[g][r]);
+#pragma unroll
+      for (int o = LPT; o < 32; o <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+      const float mn = fmaxf(st.m[g], mt);
+      if (mn > st.m[g]) {
+        const float alpha = (st.m[g] == -INFINITY) ? 0.f : exp2f(st.m[g] - mn);
+        st.l[g] *= alpha;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) st.acc[g][d] *= alpha;
+        st.m[g] = mn;
+      }
+    }
+
+    float* pw = ps + warp * TW * GP;
+#pragma unroll
+    for (int r = 0; r < TPG; ++r) {
+      float pr[GP];
+#pragma unroll
+      for (int g = 0; g < GP; ++g) {
+        pr[g] = (s[g][r] == -INFINITY) ? 0.f : exp2f(s[g][r] - st.m[g]);
+        st.l[g] += pr[g];
+      }
+      if (l8 == 0) {
+#pragma unroll
+        for (int g = 0; g < GP; ++g) pw[(r * TPW + grp) * GP + g] = pr[g];
+      }
+    }
+    __syncwarp();
+
+    const int nrow = ntok - warp * TW;
+#pragma unroll
+    for (int i = 0; i < TW; ++i) {
+      if (i < nrow) {
+        float pv[GP];
+#pragma unroll
+        for (int g = 0; g < GP; ++g) pv[g] = pw[i * GP + g];
+        float vf[DPL];
+        lds_to_f<T, DPL>(sv + (warp * TW + i) * D + lane * DPL, vf);
+#pragma unroll
+        for (int g = 0; g < GP; ++g)
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) st.acc[g][d] = fmaf(pv[g], vf[d], st.acc[g][d]);
+      }
+    }
+    __syncwarp();
+  }
+
+  __device__ static void store_state(State& s, float* ms, float* ls, float* accs) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // l holds this lane group's share; sum over the groups of the warp.
+#pragma unroll
+    for (int g = 0; g < GP; ++g)
+#pragma unroll
+      for (int o = LPT; o < 32; o <<= 1) s.l[g] += __shfl_xor_sync(0xffffffffu, s.l[g], o);
+    if (lane == 0) {
+#pragma unroll
+      for (int g = 0; g < GP; ++g) {
+        ms[warp * GP + g] = s.m[g];
+        ls[warp * GP + g] = s.l[g];
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < GP; ++g)
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) accs[(warp * GP + g) * D + lane * DPL + d] = s.acc[g][d];
+  }
+};
+
+// ===========================================================================
+// Stream-K driver
+// ===========================================================================
+template <class M>
+struct StreamK {
+  using T = typename M::T;
+  static constexpr int D = M::D, GP = M::GP, NW = M::NW, NT = M::NT;
+  static constexpr int SLOT_FLOATS = GP * (D + 2);
+  static constexpr int MERGE_FLOATS = NW * GP * (D + 2);
+  static size_t smem_bytes(int B) {
+    return (size_t)M::STAGES * M::STAGE_BYTES + (size_t)(M::EXTRA_FLOATS + MERGE_FLOATS) * 4 +
+           (size_t)(2 * B + 1 + 8) * 4;
+  }
+};
+
+template <class M>
+__global__ void __launch_bounds__(M::NT)
+attn_streamk_kernel(const AttnParams p) {
+  using T = typename M::T;
+  using SK = StreamK<M>;
+  constexpr int D = M::D, GP = M::GP, STAGES = M::STAGES, NW = M::NW, NT = M::NT;
+  constexpr int TILE = M::TILE;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  float* extra = reinterpret_cast<float*>(smem + (size_t)STAGES * M::STAGE_BYTES);
+  float* ms = extra + M::EXTRA_FLOATS;  // [NW][GP]
+  float* ls = ms + NW * GP;             // [NW][GP]
+  float* accs = ls + NW * GP;           // [NW][GP][D]
+  int* P = reinterpret_cast<int*>(accs + NW * GP * D);  // [B+1]
+  int* Ls = P + p.B + 1;                                 // [B]
+  int* misc = Ls + p.B;                                  // [8]
+  const int tid = threadIdx.x;
+  const int KVH = p.KVH;
+
+  const int64_t U = plan_units<NT>(p, P, Ls, misc);
 
   // zero-length sequences produce zeros (cuda/paged_attention.cu:56)
-  for (int b = blockIdx.x; b < B; b += gridDim.x) {
+  for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
     if (Ls[b] == 0) {
       T* o = static_cast<T*>(p.out) + (int64_t)b * p.H * D;
       for (int i = tid; i < p.H * D; i += NT) o[i] = Elem<T>::from_f(0.f);
@@ -222,66 +620,24 @@ attn_fast_kernel(const AttnParams p) {
   if (u_beg >= u_end) return;
 
   unsigned char* stages = smem;
-  const int grp = lane / LPT, l8 = lane % LPT;
-
-  // ---- loader -----------------------------------------------------------
-  auto load_tile = [&](const Cursor& c, int64_t te, int stage) {
-    const int tok0 = (int)(c.u - c.seg) * kUnitTokens;
-    const int rem = Ls[c.b] - tok0;
-    const int span = (int)(te - c.u) * kUnitTokens;
-    const int ntok = span < rem ? span : rem;
-    const int32_t* trow = p.tables + (int64_t)c.b * p.table_width;
-    unsigned char* sk = stages + (size_t)stage * Tr::STAGE_BYTES;
-    unsigned char* sv = sk + Tr::TILE_BYTES;
-#pragma unroll
-    for (int i = tid; i < TILE * CH; i += NT) {
-      const int row = i / CH, col = i % CH;
-      bool ok = row < ntok;
-      const T* ks = kpool;
-      const T* vs = vpool;
-      if (ok) {
-        const int t = tok0 + row;
-        int pi, off;
-        if (p.bs_shift >= 0) {
-          pi = t >> p.bs_shift;
-          off = t & (p.block_size - 1);
-        } else {
-          pi = t / p.block_size;
-          off = t - pi * p.block_size;
-        }
-        const int page = __ldg(trow + pi);
-        if (page < 0 || (int64_t)page >= p.num_blocks) {
-          raise_error(0x1u);
-          ok = false;
-        } else {
-          const int64_t e =
-              (((int64_t)page * p.block_size + off) * KVH + c.h) * D + col * VEC;
-          ks = kpool + e;
-          vs = vpool + e;
-        }
-      }
-      cp_async16(sk + row * Tr::ROW + col * 16, ks, ok);
-      cp_async16(sv + row * Tr::ROW + col * 16, vs, ok);
-    }
-  };
+  auto stage_k = [&](int s) { return stages + (size_t)s * M::STAGE_BYTES; };
 
   Cursor lc;
-  cursor_locate(lc, P, B, KVH, u_beg);
+  cursor_locate(lc, P, p.B, KVH, u_beg);
   Cursor cc = lc;
   bool l_done = false;
 #pragma unroll 1
   for (int s = 0; s < STAGES - 1; ++s) {
     if (!l_done) {
-      const int64_t te = cursor_tile_end<Tr::TILE_UNITS>(lc, u_end);
-      load_tile(lc, te, s);
+      const int64_t te = cursor_tile_end<M::TILE_UNITS>(lc, u_end);
+      load_tile<T, D, TILE, NT, M::SWZ>(p, Ls, lc, te, stage_k(s), stage_k(s) + M::TILE_BYTES);
       cursor_advance(lc, te, u_end, P, KVH);
       l_done = lc.u >= u_end;
     }
     cp_async_commit();
   }
 
-  float q[GP][DL];
-  float m[GP], l[GP], acc[GP][DPL];
+  typename M::State st;
   bool piece_start = true;
   int64_t piece_u0 = u_beg;
   int stage = 0, lstage = STAGES - 1;
@@ -291,158 +647,44 @@ attn_fast_kernel(const AttnParams p) {
     cp_async_wait<STAGES - 2>();
     __syncthreads();
     if (!l_done) {
-      const int64_t te = cursor_tile_end<Tr::TILE_UNITS>(lc, u_end);
-      load_tile(lc, te, lstage);
+      const int64_t te = cursor_tile_end<M::TILE_UNITS>(lc, u_end);
+      load_tile<T, D, TILE, NT, M::SWZ>(p, Ls, lc, te, stage_k(lstage),
+                                        stage_k(lstage) + M::TILE_BYTES);
       cursor_advance(lc, te, u_end, P, KVH);
       l_done = lc.u >= u_end;
     }
     cp_async_commit();
     lstage = (lstage + 1 == STAGES) ? 0 : lstage + 1;
 
-    const int64_t cte = cursor_tile_end<Tr::TILE_UNITS>(cc, u_end);
+    const int64_t cte = cursor_tile_end<M::TILE_UNITS>(cc, u_end);
     if (piece_start) {
       piece_u0 = cc.u;
       piece_start = false;
-      const T* qb = static_cast<const T*>(p.q) + ((int64_t)cc.b * p.H + (int64_t)cc.h * p.G) * D;
-#pragma unroll
-      for (int g = 0; g < GP; ++g) {
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          if (g < p.G) {
-            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qb + g * D + (l8 + LPT * c) * VEC));
-            Chunk<T>::to_f(raw, &q[g][c * VEC]);
-          } else {
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) q[g][c * VEC + e] = 0.f;
-          }
-        }
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) acc[g][d] = 0.f;
-      }
+      M::begin_piece(st, p, cc.b, cc.h);
     }
-
-    // ---- compute one tile ------------------------------------------------
-    {
-      const int tok0 = (int)(cc.u - cc.seg) * kUnitTokens;
-      const int rem = Ls[cc.b] - tok0;
-      const int span = (int)(cte - cc.u) * kUnitTokens;
-      const int ntok = span < rem ? span : rem;
-      const T* sk = reinterpret_cast<const T*>(stages + (size_t)stage * Tr::STAGE_BYTES);
-      const T* sv = reinterpret_cast<const T*>(stages + (size_t)stage * Tr::STAGE_BYTES + Tr::TILE_BYTES);
-
-      float s[GP][TPG];
-#pragma unroll
-      for (int r = 0; r < TPG; ++r) {
-        const int row = warp * TW + r * TPW + grp;
-        float part[GP];
-#pragma unroll
-        for (int g = 0; g < GP; ++g) part[g] = 0.f;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          float kf[VEC];
-          lds_to_f<T, VEC>(sk + row * D + (l8 + LPT * c) * VEC, kf);
-#pragma unroll
-          for (int g = 0; g < GP; ++g)
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) part[g] = fmaf(q[g][c * VEC + e], kf[e], part[g]);
-        }
-#pragma unroll
-        for (int o = 1; o < LPT; o <<= 1)
-#pragma unroll
-          for (int g = 0; g < GP; ++g) part[g] += __shfl_xor_sync(0xffffffffu, part[g], o);
-#pragma unroll
-        for (int g = 0; g < GP; ++g) s[g][r] = row < ntok ? part[g] * p.scale_log2 : -INFINITY;
-      }
-
-      // tile max, lazy rescale (m is warp-uniform)
-#pragma unroll
-      for (int g = 0; g < GP; ++g) {
-        float mt = s[g][0];
-#pragma unroll
-        for (int r = 1; r < TPG; ++r) mt = fmaxf(mt, s[g][r]);
-#pragma unroll
-        for (int o = LPT; o < 32; o <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-        const float mn = fmaxf(m[g], mt);
-        if (mn > m[g]) {
-          const float alpha = (m[g] == -INFINITY) ? 0.f : exp2f(m[g] - mn);
-          l[g] *= alpha;
-#pragma unroll
-          for (int d = 0; d < DPL; ++d) acc[g][d] *= alpha;
-          m[g] = mn;
-        }
-      }
-
-      float* pw = ps + warp * TW * GP;
-#pragma unroll
-      for (int r = 0; r < TPG; ++r) {
-        float pr[GP];
-#pragma unroll
-        for (int g = 0; g < GP; ++g) {
-          pr[g] = (s[g][r] == -INFINITY) ? 0.f : exp2f(s[g][r] - m[g]);
-          l[g] += pr[g];
-        }
-        if (l8 == 0) {
-#pragma unroll
-          for (int g = 0; g < GP; ++g) pw[(r * TPW + grp) * GP + g] = pr[g];
-        }
-      }
-      __syncwarp();
-
-      const int nrow = ntok - warp * TW;
-#pragma unroll
-      for (int i = 0; i < TW; ++i) {
-        if (i < nrow) {
-          float pv[GP];
-#pragma unroll
-          for (int g = 0; g < GP; ++g) pv[g] = pw[i * GP + g];
-          float vf[DPL];
-          lds_to_f<T, DPL>(sv + (warp * TW + i) * D + lane * DPL, vf);
-#pragma unroll
-          for (int g = 0; g < GP; ++g)
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) acc[g][d] = fmaf(pv[g], vf[d], acc[g][d]);
-        }
-      }
-      __syncwarp();
-    }
+    M::compute_tile(st, p, stage_k(stage), stage_k(stage) + M::TILE_BYTES,
+                    tile_tokens(cc, cte, Ls), extra);
 
     const bool seg_end = (cte == cc.seg + cc.nu);
     if (seg_end || cte == u_end) {
       // ---- finish the piece [piece_u0, cte) of segment (cc.b, cc.h) --------
-      // l holds this lane group's share; sum over the groups of the warp.
-#pragma unroll
-      for (int g = 0; g < GP; ++g)
-#pragma unroll
-        for (int o = LPT; o < 32; o <<= 1) l[g] += __shfl_xor_sync(0xffffffffu, l[g], o);
-      if (lane == 0) {
-#pragma unroll
-        for (int g = 0; g < GP; ++g) {
-          ms[warp * GP + g] = m[g];
-          ls[warp * GP + g] = l[g];
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < GP; ++g)
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) accs[(warp * GP + g) * D + lane * DPL + d] = acc[g][d];
+      M::store_state(st, ms, ls, accs);
       __syncthreads();
 
       const bool whole = (piece_u0 == cc.seg) && seg_end;
       T* outp = static_cast<T*>(p.out) + ((int64_t)cc.b * p.H + (int64_t)cc.h * p.G) * D;
       float* slot = p.partials +
-                    (size_t)(2 * blockIdx.x + (piece_u0 == u_beg ? 0 : 1)) * Tr::SLOT_FLOATS;
+                    (size_t)(2 * blockIdx.x + (piece_u0 == u_beg ? 0 : 1)) * SK::SLOT_FLOATS;
       for (int idx = tid; idx < GP * D; idx += NT) {
         const int g = idx / D, d = idx - g * D;
-        float M = -INFINITY;
+        float M_ = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, ms[w * GP + g]);
+        for (int w = 0; w < NW; ++w) M_ = fmaxf(M_, ms[w * GP + g]);
         float L = 0.f, O = 0.f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
           const float mw = ms[w * GP + g];
-          const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+          const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M_);
           L = fmaf(ls[w * GP + g], f, L);
           O = fmaf(accs[(w * GP + g) * D + d], f, O);
         }
@@ -451,7 +693,7 @@ attn_fast_kernel(const AttnParams p) {
         } else {
           slot[2 * GP + g * D + d] = O;
           if (d == 0) {
-            slot[g] = M;
+            slot[g] = M_;
             slot[GP + g] = L;
           }
         }
@@ -464,6 +706,8 @@ attn_fast_kernel(const AttnParams p) {
         const int64_t c0 = part_owner(S0, U, grid), c1 = part_owner(S1 - 1, U, grid);
         unsigned long long* ctr = p.counters + ((int64_t)cc.b * KVH + cc.h);
         if (tid == 0) {
+          // Arrive: one CAS loop, bounded (each failure means another piece of
+          // this segment arrived, so at most pieces-1 retries are possible).
           const unsigned long long ep = (unsigned long long)p.epoch << 32;
           unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
           int last = 0;
@@ -487,18 +731,18 @@ attn_fast_kernel(const AttnParams p) {
           for (int idx = tid; idx < GP * D; idx += NT) {
             const int g = idx / D, d = idx - g * D;
             if (g >= p.G) continue;
-            float M = -INFINITY;
+            float M_ = -INFINITY;
             for (int64_t c = c0; c <= c1; ++c) {
               const float* sl = p.partials +
-                  (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * Tr::SLOT_FLOATS;
-              M = fmaxf(M, __ldcg(sl + g));
+                  (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * SK::SLOT_FLOATS;
+              M_ = fmaxf(M_, __ldcg(sl + g));
             }
             float L = 0.f, O = 0.f;
             for (int64_t c = c0; c <= c1; ++c) {
               const float* sl = p.partials +
-                  (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * Tr::SLOT_FLOATS;
+                  (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * SK::SLOT_FLOATS;
               const float mc = __ldcg(sl + g);
-              const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M);
+              const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M_);
               L = fmaf(__ldcg(sl + GP + g), f, L);
               O = fmaf(__ldcg(sl + 2 * GP + g * D + d), f, O);
             }
@@ -519,7 +763,7 @@ attn_fast_kernel(const AttnParams p) {
 }
 
 // ===========================================================================
-// Generic kernel (fallback for shapes outside the fast instantiations)
+// Generic kernel (fallback for shapes outside the stream-K instantiations)
 // ===========================================================================
 template <typename T>
 __global__ void __launch_bounds__(128) attn_generic_kernel(const AttnParams p) {

@@ -83,67 +83,92 @@ uint32_t next_epoch() {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// ---- fast kernel registry ---------------------------------------------------
+// ---- stream-K kernel registry -----------------------------------------------
 struct FastKernel {
   const void* fn;
   void (*launch)(const pdb::AttnParams&, int grid, size_t smem, cudaStream_t);
   size_t (*smem)(int B);
-  int gp;
+  int gp;  // heads per kv head kept in partial slots
 };
 
-template <class Tr>
-void launch_fast(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st) {
-  pdb::attn_fast_kernel<Tr><<<grid, Tr::NT, smem, st>>>(p);
+template <class M>
+void launch_streamk(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st) {
+  pdb::attn_streamk_kernel<M><<<grid, M::NT, smem, st>>>(p);
 }
 
-template <class Tr>
+template <class M>
 FastKernel make_fast() {
-  return FastKernel{reinterpret_cast<const void*>(&pdb::attn_fast_kernel<Tr>), &launch_fast<Tr>,
-                    &Tr::smem_bytes, Tr::GP};
+  return FastKernel{reinterpret_cast<const void*>(&pdb::attn_streamk_kernel<M>),
+                    &launch_streamk<M>, &pdb::StreamK<M>::smem_bytes, M::GP};
 }
 
-// Tile depth per (dtype, head_dim): ~16 KB (fp16) / 32 KB (fp32) stages.
+// SIMT inner loop: tile depth per (dtype, head_dim), ~16 KB (fp16) / 32 KB
+// (fp32) per stage.
 template <typename T, int D, int GP>
-FastKernel fast_for() {
+FastKernel simt_for() {
   if constexpr (sizeof(T) == 2) {
-    if constexpr (D == 128) return make_fast<pdb::FastTraits<T, D, GP, 2, 4>>();
-    else return make_fast<pdb::FastTraits<T, D, GP, 2, 6>>();
+    if constexpr (D == 128) return make_fast<pdb::SimtMath<T, D, GP, 2, 4>>();
+    else return make_fast<pdb::SimtMath<T, D, GP, 2, 6>>();
   } else {
-    if constexpr (D == 128) return make_fast<pdb::FastTraits<T, D, GP, 2, 3>>();
-    else if constexpr (D == 64) return make_fast<pdb::FastTraits<T, D, GP, 2, 4>>();
-    else return make_fast<pdb::FastTraits<T, D, GP, 2, 6>>();
+    if constexpr (D == 128) return make_fast<pdb::SimtMath<T, D, GP, 2, 3>>();
+    else if constexpr (D == 64) return make_fast<pdb::SimtMath<T, D, GP, 2, 4>>();
+    else return make_fast<pdb::SimtMath<T, D, GP, 2, 6>>();
   }
 }
 
 template <typename T, int D>
-bool pick_gp(int G, FastKernel* out) {
-  if (G <= 1) { *out = fast_for<T, D, 1>(); return true; }
-  if (G <= 2) { *out = fast_for<T, D, 2>(); return true; }
-  if (G <= 4) { *out = fast_for<T, D, 4>(); return true; }
+bool pick_simt_gp(int G, FastKernel* out) {
+  if (G <= 1) { *out = simt_for<T, D, 1>(); return true; }
+  if (G <= 2) { *out = simt_for<T, D, 2>(); return true; }
+  if (G <= 4) { *out = simt_for<T, D, 4>(); return true; }
   if constexpr (D <= 64) {
-    if (G <= 8) { *out = fast_for<T, D, 8>(); return true; }
+    if (G <= 8) { *out = simt_for<T, D, 8>(); return true; }
   }
   return false;
 }
 
 template <typename T>
-bool pick_fast_t(int D, int G, FastKernel* out) {
+bool pick_simt(int D, int G, FastKernel* out) {
   switch (D) {
-    case 32: return pick_gp<T, 32>(G, out);
-    case 64: return pick_gp<T, 64>(G, out);
-    case 128: return pick_gp<T, 128>(G, out);
+    case 32: return pick_simt_gp<T, 32>(G, out);
+    case 64: return pick_simt_gp<T, 64>(G, out);
+    case 128: return pick_simt_gp<T, 128>(G, out);
     default: return false;
   }
 }
 
+// Tensor-core inner loop (FP16): 64-token tiles (32 KB per stage at D 128).
+bool pick_mma(int D, int G, FastKernel* out) {
+  if (G > 8) return false;
+  const bool g4 = G <= 4;
+  if (D == 128) {
+    *out = g4 ? make_fast<pdb::MmaMath<128, 4, 3>>() : make_fast<pdb::MmaMath<128, 8, 2>>();
+    return true;
+  }
+  if (D == 64) {
+    *out = g4 ? make_fast<pdb::MmaMath<64, 4, 4>>() : make_fast<pdb::MmaMath<64, 8, 4>>();
+    return true;
+  }
+  return false;
+}
+
 constexpr int kFastMaxBatch = 4096;
 
-bool fast_applicable(int64_t B, int64_t H, int64_t KVH, int64_t D, int dtype, FastKernel* k) {
-  if (B > kFastMaxBatch) return false;
-  if (B * KVH * (8192 / pdb::kUnitTokens) >= (int64_t(1) << 31)) return false;
+bool streamk_shape_ok(int64_t B, int64_t KVH) {
+  return B <= kFastMaxBatch && B * KVH * (8192 / pdb::kUnitTokens) < (int64_t(1) << 31);
+}
+
+// The stream-K kernel for this shape: tensor cores for FP16 where they
+// apply (unless `simt_only`), else the SIMT inner loop.
+bool fast_applicable(int64_t B, int64_t H, int64_t KVH, int64_t D, int dtype, FastKernel* k,
+                     bool simt_only = false) {
+  if (!streamk_shape_ok(B, KVH)) return false;
   const int G = (int)(H / KVH);
-  return dtype == PDB_DTYPE_FLOAT16 ? pick_fast_t<__half>((int)D, G, k)
-                                    : pick_fast_t<float>((int)D, G, k);
+  if (dtype == PDB_DTYPE_FLOAT16) {
+    if (!simt_only && pick_mma((int)D, G, k)) return true;
+    return pick_simt<__half>((int)D, G, k);
+  }
+  return pick_simt<float>((int)D, G, k);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -255,7 +280,7 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
   if (rc) return rc;
   if (!q || !k_pool || !v_pool || !tables || !lengths || !out)
     return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  if (impl < PDB_IMPL_AUTO || impl > PDB_IMPL_GENERIC)
+  if (impl < PDB_IMPL_AUTO || impl > PDB_IMPL_SIMT)
     return fail(PDB_ERR_INVALID_ARGUMENT, "unknown kernel selection");
   int dev = 0;
   if ((rc = current_device(&dev))) return rc;
@@ -275,9 +300,9 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
     return fail(PDB_ERR_WORKSPACE, "workspace must be 256-byte aligned");
 
   FastKernel fk;
-  const bool fast_ok = fast_applicable(B, H, KVH, D, dtype, &fk) && aligned16(q) &&
-                       aligned16(k_pool) && aligned16(v_pool);
-  if (impl == PDB_IMPL_FAST && !fast_ok)
+  const bool fast_ok = fast_applicable(B, H, KVH, D, dtype, &fk, impl == PDB_IMPL_SIMT) &&
+                       aligned16(q) && aligned16(k_pool) && aligned16(v_pool);
+  if ((impl == PDB_IMPL_FAST || impl == PDB_IMPL_SIMT) && !fast_ok)
     return fail(PDB_ERR_INVALID_ARGUMENT, "fast kernel does not support this shape/alignment");
 
   if (fast_ok && impl != PDB_IMPL_GENERIC) {

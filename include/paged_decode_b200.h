@@ -54,9 +54,11 @@ typedef enum {
 
 /* Kernel selection for pdb_paged_attention_impl. */
 typedef enum {
-  PDB_IMPL_AUTO = 0,    /* fast kernel when the shape allows, else generic   */
-  PDB_IMPL_FAST = 1,    /* GQA-shared, cp.async-staged, stream-K split       */
-  PDB_IMPL_GENERIC = 2  /* any head_dim <= 256 / any alignment, split + combine */
+  PDB_IMPL_AUTO = 0,    /* stream-K kernel when the shape allows, else generic  */
+  PDB_IMPL_FAST = 1,    /* stream-K, GQA-shared tiles: tensor cores for FP16
+                           head_dim 64/128, SIMT otherwise                     */
+  PDB_IMPL_GENERIC = 2, /* any head_dim <= 256 / any alignment, split + combine */
+  PDB_IMPL_SIMT = 3     /* stream-K with the SIMT inner loop only               */
 } pdb_impl_t;
 
 /* Bits of the per-device error word (pdb_read_device_errors). */

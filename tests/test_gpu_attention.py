@@ -17,7 +17,8 @@ pytestmark = pytest.mark.gpu
 mg = golden_module()
 W = import_module("workloads")
 _lib = import_module("_lib")
-IMPLS = [_lib.IMPL_AUTO, _lib.IMPL_FAST, _lib.IMPL_GENERIC]
+IMPLS = [_lib.IMPL_AUTO, _lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT]
+STREAMK = (_lib.IMPL_FAST, _lib.IMPL_SIMT)
 
 
 def gold(name):
@@ -29,8 +30,8 @@ def run(pkg, q, k, v, tables, lengths, max_length, impl, dev):
         out = pkg.paged_attention(q.to(dev), k.to(dev), v.to(dev), tables.to(dev),
                                   lengths.to(dev), max_length, impl=impl)
     except RuntimeError as e:
-        if impl == _lib.IMPL_FAST and "fast kernel does not support" in str(e):
-            pytest.skip("shape outside the fast kernel's instantiations")
+        if impl in STREAMK and "fast kernel does not support" in str(e):
+            pytest.skip("shape outside the stream-K kernel's instantiations")
         raise
     torch.cuda.synchronize()
     return out.cpu()
@@ -55,7 +56,7 @@ def test_edge_cases(pkg, cuda, impl):
             out = pkg.paged_attention(q.to(cuda), k.to(cuda), v.to(cuda), tables.to(cuda),
                                       lengths.to(cuda), max_len, impl=impl).cpu()
         except RuntimeError as e:
-            if impl == _lib.IMPL_FAST and "fast kernel does not support" in str(e):
+            if impl in STREAMK and "fast kernel does not support" in str(e):
                 continue
             raise
         assert_parity(out, case["out"], case["spec"]["name"])
@@ -84,7 +85,7 @@ def test_stale_pool_bytes_are_never_read(pkg, cuda, dtype, impl):
     assert torch.equal(clean, poisoned)
 
 
-@pytest.mark.parametrize("impl", [_lib.IMPL_FAST, _lib.IMPL_GENERIC])
+@pytest.mark.parametrize("impl", [_lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT])
 def test_repeated_calls_are_deterministic(pkg, cuda, impl):
     w = W.llama3_8b(batch=24, layers=1)
     t = W.materialize(w, cuda)
@@ -107,16 +108,17 @@ def test_smollm_fp16_layer(pkg, cuda):
 
 
 def test_llama3_full_batch(pkg, cuda):
-    """Llama-3-8B shape at the full batch of 256, one layer: the two kernels
-    agree everywhere, and 12 sequences (shortest, longest, random) match the
-    CPU oracle."""
+    """Llama-3-8B shape at the full batch of 256, one layer: the three kernels
+    (tensor-core stream-K, SIMT stream-K, generic split) agree everywhere, and
+    12 sequences (shortest, longest, random) match the CPU oracle."""
     w = W.llama3_8b(layers=1)
     t = W.materialize(w, cuda)
-    fast = pkg.paged_attention(t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths,
-                               w.max_length, impl=_lib.IMPL_FAST)
-    generic = pkg.paged_attention(t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths,
-                                  w.max_length, impl=_lib.IMPL_GENERIC)
-    assert_parity(fast, generic.cpu(), "fast vs generic")
+    args = (t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths, w.max_length)
+    fast = pkg.paged_attention(*args, impl=_lib.IMPL_FAST)
+    generic = pkg.paged_attention(*args, impl=_lib.IMPL_GENERIC)
+    simt = pkg.paged_attention(*args, impl=_lib.IMPL_SIMT)
+    assert_parity(fast, generic.cpu(), "tensor-core vs generic")
+    assert_parity(simt, generic.cpu(), "simt vs generic")
     order = torch.argsort(w.lengths)
     pick = torch.cat([order[:3], order[-3:], torch.randperm(w.batch, generator=torch.Generator().manual_seed(0))[:6]])
     pick = pick.unique()
