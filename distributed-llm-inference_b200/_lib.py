@@ -40,7 +40,7 @@ SIGNATURES = {
 
 DTYPE_FLOAT32 = 0
 DTYPE_FLOAT16 = 1
-IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT = 0, 1, 2, 3
+IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA = 0, 1, 2, 3, 4
 STATUS_NAMES = {0: "ok", 1: "invalid argument", 2: "workspace", 3: "cuda"}
 
 _lock = threading.Lock()

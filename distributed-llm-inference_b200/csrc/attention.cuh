@@ -266,10 +266,18 @@ __device__ __forceinline__ void load_tile(const AttnParams& p, const int* Ls, co
 // ===========================================================================
 // GQ: query heads of the group that are kept (4 or 8); the MMA N dimension
 // always computes 8 columns, columns >= G see q = 0 and are never stored.
-template <int D_, int GQ_, int STAGES_>
+// Staged-tile layouts read by MmaMath:
+//   kRowSwizzle  one D*2-byte row per token, 16-byte chunks XOR (row & 7)
+//                (written by cp.async);
+//   kTma128B     the tile split into D/64 column halves of 128-byte rows,
+//                each [TILE rows x 128 B] with the TMA 128-byte swizzle
+//                (chunk XOR (row & 7)); written by cp.async.bulk.tensor.
+enum : int { kRowSwizzle = 0, kTma128B = 1 };
+
+template <int D_, int GQ_, int STAGES_, int LAYOUT_ = kRowSwizzle>
 struct MmaMath {
   using T = __half;
-  static constexpr int D = D_, GP = GQ_, STAGES = STAGES_;
+  static constexpr int D = D_, GP = GQ_, STAGES = STAGES_, LAYOUT = LAYOUT_;
   static constexpr int NW = 4, NT = 128;
   static constexpr int WT = 16;          // tokens per warp per tile (MMA M)
   static constexpr int TILE = NW * WT;   // 64 tokens
@@ -282,6 +290,15 @@ struct MmaMath {
   static constexpr int EXTRA_FLOATS = 0;
   static_assert(D % 64 == 0, "swizzle needs >= 8 chunks per row");
   static_assert(GQ_ == 4 || GQ_ == 8, "group");
+
+  // Byte offset of 16-byte chunk `col` (0..D/8-1) of token row `row`.
+  __device__ static __forceinline__ int offset(int row, int col) {
+    if constexpr (LAYOUT == kTma128B) {
+      return (col >> 3) * (TILE * 128) + row * 128 + (((col & 7) ^ (row & 7)) << 4);
+    } else {
+      return tile_offset<ROW, true>(row, col);
+    }
+  }
 
   struct State {
     uint32_t qb[KSTEPS][2];  // B fragments of Q^T (8 heads)
@@ -321,7 +338,7 @@ struct MmaMath {
 #pragma unroll
       for (int ks = 0; ks < KSTEPS; ++ks) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4(a0, a1, a2, a3, sk + tile_offset<ROW, true>(row, 2 * ks + (mi >> 1)));
+        ldsm_x4(a0, a1, a2, a3, sk + offset(row, 2 * ks + (mi >> 1)));
         mma_16816((ks & 1) ? c1 : c0, a0, a1, a2, a3, s.qb[ks][0], s.qb[ks][1]);
       }
     }
@@ -373,7 +390,7 @@ struct MmaMath {
 #pragma unroll
     for (int md = 0; md < KSTEPS; ++md) {
       uint32_t a0, a1, a2, a3;
-      ldsm_x4_t(a0, a1, a2, a3, sv + tile_offset<ROW, true>(vrow, 2 * md + (mi & 1)));
+      ldsm_x4_t(a0, a1, a2, a3, sv + offset(vrow, 2 * md + (mi & 1)));
       mma_16816(s.acc[md], a0, a1, a2, a3, bh0, bh1);
       mma_16816(s.acc[md], a0, a1, a2, a3, bl0, bl1);
     }
@@ -582,6 +599,103 @@ struct StreamK {
   }
 };
 
+// Merge the NW warp states of a finished piece [piece_u0, ...) of segment
+// (cc.b, cc.h) and write the output, or publish the piece's partial and, if
+// this CTA is the last to finish a piece of the segment, combine all pieces.
+// `sync` is a barrier over the threads that call this (all math warps).
+// On entry the warp states are in ms/ls/accs and `sync` has been passed.
+template <class M, class Sync>
+__device__ __forceinline__ void finish_piece(const AttnParams& p, const Cursor& cc,
+                                             int64_t piece_u0, int64_t u_beg, int64_t U,
+                                             int64_t grid, bool seg_end, const float* ms,
+                                             const float* ls, const float* accs, int* misc,
+                                             Sync sync) {
+  using T = typename M::T;
+  constexpr int D = M::D, GP = M::GP, NW = M::NW, NT = M::NT;
+  constexpr int SLOT_FLOATS = GP * (D + 2);
+  const int tid = threadIdx.x;
+  const bool whole = (piece_u0 == cc.seg) && seg_end;
+  T* outp = static_cast<T*>(p.out) + ((int64_t)cc.b * p.H + (int64_t)cc.h * p.G) * D;
+  float* slot = p.partials + (size_t)(2 * blockIdx.x + (piece_u0 == u_beg ? 0 : 1)) * SLOT_FLOATS;
+  for (int idx = tid; idx < GP * D; idx += NT) {
+    const int g = idx / D, d = idx - g * D;
+    float M_ = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M_ = fmaxf(M_, ms[w * GP + g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float mw = ms[w * GP + g];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M_);
+      L = fmaf(ls[w * GP + g], f, L);
+      O = fmaf(accs[(w * GP + g) * D + d], f, O);
+    }
+    if (whole) {
+      if (g < p.G) outp[g * D + d] = Elem<T>::from_f(O / L);
+    } else {
+      slot[2 * GP + g * D + d] = O;
+      if (d == 0) {
+        slot[g] = M_;
+        slot[GP + g] = L;
+      }
+    }
+  }
+
+  if (!whole) {
+    __threadfence();
+    sync();
+    const int64_t S0 = cc.seg, S1 = cc.seg + cc.nu;
+    const int64_t c0 = part_owner(S0, U, grid), c1 = part_owner(S1 - 1, U, grid);
+    unsigned long long* ctr = p.counters + ((int64_t)cc.b * p.KVH + cc.h);
+    if (tid == 0) {
+      // Arrive: one CAS loop, bounded (each failure means another piece of
+      // this segment arrived, so at most pieces-1 retries are possible).
+      const unsigned long long ep = (unsigned long long)p.epoch << 32;
+      unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
+      int last = 0;
+      bool done = false;
+      for (int it = 0; it < (1 << 20) && !done; ++it) {
+        const unsigned cnt = ((old >> 32) == p.epoch) ? (unsigned)(old & 0xffffffffull) : 0u;
+        const unsigned long long nw = ep | (unsigned long long)(cnt + 1u);
+        const unsigned long long prev = atomicCAS(ctr, old, nw);
+        if (prev == old) {
+          done = true;
+          last = ((int64_t)cnt + 1 == c1 - c0 + 1) ? 1 : 0;
+        } else {
+          old = prev;
+        }
+      }
+      misc[1] = last;
+    }
+    sync();
+    if (misc[1]) {
+      __threadfence();
+      for (int idx = tid; idx < GP * D; idx += NT) {
+        const int g = idx / D, d = idx - g * D;
+        if (g >= p.G) continue;
+        float M_ = -INFINITY;
+        for (int64_t c = c0; c <= c1; ++c) {
+          const float* sl = p.partials +
+              (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * SLOT_FLOATS;
+          M_ = fmaxf(M_, __ldcg(sl + g));
+        }
+        float L = 0.f, O = 0.f;
+        for (int64_t c = c0; c <= c1; ++c) {
+          const float* sl = p.partials +
+              (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * SLOT_FLOATS;
+          const float mc = __ldcg(sl + g);
+          const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M_);
+          L = fmaf(__ldcg(sl + GP + g), f, L);
+          O = fmaf(__ldcg(sl + 2 * GP + g * D + d), f, O);
+        }
+        outp[g * D + d] = Elem<T>::from_f(O / L);
+      }
+      if (tid == 0) atomicExch(ctr, (unsigned long long)p.epoch << 32);
+    }
+  }
+  sync();
+}
+
 template <class M>
 __global__ void __launch_bounds__(M::NT)
 attn_streamk_kernel(const AttnParams p) {
@@ -667,91 +781,10 @@ attn_streamk_kernel(const AttnParams p) {
 
     const bool seg_end = (cte == cc.seg + cc.nu);
     if (seg_end || cte == u_end) {
-      // ---- finish the piece [piece_u0, cte) of segment (cc.b, cc.h) --------
       M::store_state(st, ms, ls, accs);
       __syncthreads();
-
-      const bool whole = (piece_u0 == cc.seg) && seg_end;
-      T* outp = static_cast<T*>(p.out) + ((int64_t)cc.b * p.H + (int64_t)cc.h * p.G) * D;
-      float* slot = p.partials +
-                    (size_t)(2 * blockIdx.x + (piece_u0 == u_beg ? 0 : 1)) * SK::SLOT_FLOATS;
-      for (int idx = tid; idx < GP * D; idx += NT) {
-        const int g = idx / D, d = idx - g * D;
-        float M_ = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) M_ = fmaxf(M_, ms[w * GP + g]);
-        float L = 0.f, O = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          const float mw = ms[w * GP + g];
-          const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M_);
-          L = fmaf(ls[w * GP + g], f, L);
-          O = fmaf(accs[(w * GP + g) * D + d], f, O);
-        }
-        if (whole) {
-          if (g < p.G) outp[g * D + d] = Elem<T>::from_f(O / L);
-        } else {
-          slot[2 * GP + g * D + d] = O;
-          if (d == 0) {
-            slot[g] = M_;
-            slot[GP + g] = L;
-          }
-        }
-      }
-
-      if (!whole) {
-        __threadfence();
-        __syncthreads();
-        const int64_t S0 = cc.seg, S1 = cc.seg + cc.nu;
-        const int64_t c0 = part_owner(S0, U, grid), c1 = part_owner(S1 - 1, U, grid);
-        unsigned long long* ctr = p.counters + ((int64_t)cc.b * KVH + cc.h);
-        if (tid == 0) {
-          // Arrive: one CAS loop, bounded (each failure means another piece of
-          // this segment arrived, so at most pieces-1 retries are possible).
-          const unsigned long long ep = (unsigned long long)p.epoch << 32;
-          unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
-          int last = 0;
-          bool done = false;
-          for (int it = 0; it < (1 << 20) && !done; ++it) {
-            const unsigned cnt = ((old >> 32) == p.epoch) ? (unsigned)(old & 0xffffffffull) : 0u;
-            const unsigned long long nw = ep | (unsigned long long)(cnt + 1u);
-            const unsigned long long prev = atomicCAS(ctr, old, nw);
-            if (prev == old) {
-              done = true;
-              last = ((int64_t)cnt + 1 == c1 - c0 + 1) ? 1 : 0;
-            } else {
-              old = prev;
-            }
-          }
-          misc[1] = last;
-        }
-        __syncthreads();
-        if (misc[1]) {
-          __threadfence();
-          for (int idx = tid; idx < GP * D; idx += NT) {
-            const int g = idx / D, d = idx - g * D;
-            if (g >= p.G) continue;
-            float M_ = -INFINITY;
-            for (int64_t c = c0; c <= c1; ++c) {
-              const float* sl = p.partials +
-                  (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * SK::SLOT_FLOATS;
-              M_ = fmaxf(M_, __ldcg(sl + g));
-            }
-            float L = 0.f, O = 0.f;
-            for (int64_t c = c0; c <= c1; ++c) {
-              const float* sl = p.partials +
-                  (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * SK::SLOT_FLOATS;
-              const float mc = __ldcg(sl + g);
-              const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M_);
-              L = fmaf(__ldcg(sl + GP + g), f, L);
-              O = fmaf(__ldcg(sl + 2 * GP + g * D + d), f, O);
-            }
-            outp[g * D + d] = Elem<T>::from_f(O / L);
-          }
-          if (tid == 0) atomicExch(ctr, (unsigned long long)p.epoch << 32);
-        }
-      }
-      __syncthreads();
+      finish_piece<M>(p, cc, piece_u0, u_beg, U, grid, seg_end, ms, ls, accs, misc,
+                      [] { __syncthreads(); });
       piece_start = true;
     }
 

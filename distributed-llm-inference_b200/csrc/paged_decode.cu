@@ -12,8 +12,11 @@
 #include <string>
 #include <tuple>
 
-#include "../../include/paged_decode_b200.h"
+#include <cudaTypedefs.h>
+
+#include "paged_decode_b200.h"
 #include "attention.cuh"
+#include "attention_tma.cuh"
 #include "rope_kv_write.cuh"
 
 namespace {
@@ -86,20 +89,68 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // ---- stream-K kernel registry -----------------------------------------------
 struct FastKernel {
   const void* fn;
-  void (*launch)(const pdb::AttnParams&, int grid, size_t smem, cudaStream_t);
+  void (*launch)(const pdb::AttnParams&, int grid, size_t smem, cudaStream_t,
+                 const CUtensorMap* kmap, const CUtensorMap* vmap);
   size_t (*smem)(int B);
-  int gp;  // heads per kv head kept in partial slots
+  int gp;       // heads per kv head kept in partial slots
+  int threads;  // CTA size
+  bool tma;     // needs K/V tensor maps
 };
 
 template <class M>
-void launch_streamk(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st) {
+void launch_streamk(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st,
+                    const CUtensorMap*, const CUtensorMap*) {
   pdb::attn_streamk_kernel<M><<<grid, M::NT, smem, st>>>(p);
 }
 
 template <class M>
 FastKernel make_fast() {
   return FastKernel{reinterpret_cast<const void*>(&pdb::attn_streamk_kernel<M>),
-                    &launch_streamk<M>, &pdb::StreamK<M>::smem_bytes, M::GP};
+                    &launch_streamk<M>, &pdb::StreamK<M>::smem_bytes, M::GP, M::NT, false};
+}
+
+template <class M>
+void launch_tma(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st,
+                const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  pdb::attn_tma_kernel<M><<<grid, pdb::TmaStreamK<M>::NT, smem, st>>>(p, *kmap, *vmap);
+}
+
+template <class M>
+FastKernel make_tma() {
+  return FastKernel{reinterpret_cast<const void*>(&pdb::attn_tma_kernel<M>), &launch_tma<M>,
+                    &pdb::TmaStreamK<M>::smem_bytes, M::GP, pdb::TmaStreamK<M>::NT, true};
+}
+
+// cuTensorMapEncodeTiled from the driver (resolved once through the runtime,
+// so the library needs no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      ptr = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+// Pool [N, bs, KVH, D] (FP16) viewed as [N*bs rows, KVH, D]; box = one
+// 16-token unit of one kv head, 64 columns, 128-byte swizzle.
+bool encode_pool_map(CUtensorMap* m, const void* pool, int64_t N, int64_t bs, int64_t KVH,
+                     int64_t D) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)KVH, (cuuint64_t)(N * bs)};
+  const cuuint64_t strides[2] = {(cuuint64_t)(D * 2), (cuuint64_t)(KVH * D * 2)};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)pdb::kUnitTokens};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(pool), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // SIMT inner loop: tile depth per (dtype, head_dim), ~16 KB (fp16) / 32 KB
@@ -137,6 +188,24 @@ bool pick_simt(int D, int G, FastKernel* out) {
   }
 }
 
+// Tensor-core inner loop with a TMA producer warp (FP16, block_size % 16 == 0).
+// Stage depths keep two CTAs resident per SM.
+bool pick_tma(int D, int G, FastKernel* out) {
+  if (G > 8) return false;
+  const bool g4 = G <= 4;
+  if (D == 128) {
+    *out = g4 ? make_tma<pdb::MmaMath<128, 4, 3, pdb::kTma128B>>()
+              : make_tma<pdb::MmaMath<128, 8, 2, pdb::kTma128B>>();
+    return true;
+  }
+  if (D == 64) {
+    *out = g4 ? make_tma<pdb::MmaMath<64, 4, 6, pdb::kTma128B>>()
+              : make_tma<pdb::MmaMath<64, 8, 5, pdb::kTma128B>>();
+    return true;
+  }
+  return false;
+}
+
 // Tensor-core inner loop (FP16): 64-token tiles (32 KB per stage at D 128).
 bool pick_mma(int D, int G, FastKernel* out) {
   if (G > 8) return false;
@@ -158,16 +227,27 @@ bool streamk_shape_ok(int64_t B, int64_t KVH) {
   return B <= kFastMaxBatch && B * KVH * (8192 / pdb::kUnitTokens) < (int64_t(1) << 31);
 }
 
-// The stream-K kernel for this shape: tensor cores for FP16 where they
-// apply (unless `simt_only`), else the SIMT inner loop.
+// Kernel families a caller can pin (pdb_impl_t) below AUTO/FAST.
+enum Family { kAny = 0, kSimtOnly = 1, kCpAsyncMma = 2 };
+
+// The stream-K kernel for this shape: FP16 tensor cores fed by TMA when the
+// pool allows (block_size % 16 == 0, rows addressable by 32-bit coordinates,
+// driver encoder present), tensor cores fed by cp.async otherwise, the SIMT
+// inner loop for FP32 and the remaining FP16 shapes. `bs`/`N` = 0 skips the
+// TMA conditions (workspace sizing, where every candidate needs the same slots).
 bool fast_applicable(int64_t B, int64_t H, int64_t KVH, int64_t D, int dtype, FastKernel* k,
-                     bool simt_only = false) {
+                     int family = kAny, int64_t bs = 16, int64_t N = 1) {
   if (!streamk_shape_ok(B, KVH)) return false;
   const int G = (int)(H / KVH);
   if (dtype == PDB_DTYPE_FLOAT16) {
-    if (!simt_only && pick_mma((int)D, G, k)) return true;
+    if (family == kAny && bs % pdb::kUnitTokens == 0 && N * bs < (int64_t(1) << 31) &&
+        tensor_map_encoder() && pick_tma((int)D, G, k))
+      return true;
+    if (family != kSimtOnly && pick_mma((int)D, G, k)) return true;
+    if (family == kCpAsyncMma) return false;
     return pick_simt<__half>((int)D, G, k);
   }
+  if (family == kCpAsyncMma) return false;
   return pick_simt<float>((int)D, G, k);
 }
 
@@ -177,7 +257,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // than the upper bound on 16-token units.
 int64_t fast_grid(int dev, const FastKernel& k, int64_t B, int64_t KVH, int64_t max_length) {
   const size_t smem = k.smem((int)B);
-  const int occ = ctas_per_sm(dev, k.fn, smem, 128);
+  const int occ = ctas_per_sm(dev, k.fn, smem, k.threads);
   const int sms = sm_count(dev);
   if (occ <= 0 || sms <= 0) return 0;
   int64_t grid = (int64_t)occ * sms;
@@ -247,13 +327,27 @@ size_t pdb_paged_attention_workspace_size(int64_t batch, int64_t heads, int64_t 
       max_length <= 0)
     return 0;
   size_t need = generic_ws(batch, heads, head_dim, generic_splits(max_length));
-  FastKernel k;
   int dev = 0;
-  if (fast_applicable(batch, heads, kv_heads, head_dim, dtype, &k) &&
-      cudaGetDevice(&dev) == cudaSuccess) {
-    const int64_t grid = fast_grid(dev, k, batch, kv_heads, max_length);
+  if (!streamk_shape_ok(batch, kv_heads) || cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return need;
+  }
+  // The pool's block size is not known here, so cover every stream-K kernel
+  // that a call of this shape may select.
+  const int G = (int)(heads / kv_heads);
+  FastKernel cand[3];
+  int n = 0;
+  if (dtype == PDB_DTYPE_FLOAT16) {
+    if (tensor_map_encoder() && pick_tma((int)head_dim, G, &cand[n])) ++n;
+    if (pick_mma((int)head_dim, G, &cand[n])) ++n;
+    if (pick_simt<__half>((int)head_dim, G, &cand[n])) ++n;
+  } else if (pick_simt<float>((int)head_dim, G, &cand[n])) {
+    ++n;
+  }
+  for (int i = 0; i < n; ++i) {
+    const int64_t grid = fast_grid(dev, cand[i], batch, kv_heads, max_length);
     if (grid > 0) {
-      const size_t f = fast_ws_layout(batch, kv_heads, head_dim, k.gp, grid).total;
+      const size_t f = fast_ws_layout(batch, kv_heads, head_dim, cand[i].gp, grid).total;
       if (f > need) need = f;
     }
   }
@@ -280,7 +374,7 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
   if (rc) return rc;
   if (!q || !k_pool || !v_pool || !tables || !lengths || !out)
     return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  if (impl < PDB_IMPL_AUTO || impl > PDB_IMPL_SIMT)
+  if (impl < PDB_IMPL_AUTO || impl > PDB_IMPL_MMA)
     return fail(PDB_ERR_INVALID_ARGUMENT, "unknown kernel selection");
   int dev = 0;
   if ((rc = current_device(&dev))) return rc;
@@ -300,9 +394,10 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
     return fail(PDB_ERR_WORKSPACE, "workspace must be 256-byte aligned");
 
   FastKernel fk;
-  const bool fast_ok = fast_applicable(B, H, KVH, D, dtype, &fk, impl == PDB_IMPL_SIMT) &&
+  const int family = impl == PDB_IMPL_SIMT ? kSimtOnly : impl == PDB_IMPL_MMA ? kCpAsyncMma : kAny;
+  const bool fast_ok = fast_applicable(B, H, KVH, D, dtype, &fk, family, bs, N) &&
                        aligned16(q) && aligned16(k_pool) && aligned16(v_pool);
-  if ((impl == PDB_IMPL_FAST || impl == PDB_IMPL_SIMT) && !fast_ok)
+  if (impl != PDB_IMPL_AUTO && impl != PDB_IMPL_GENERIC && !fast_ok)
     return fail(PDB_ERR_INVALID_ARGUMENT, "fast kernel does not support this shape/alignment");
 
   if (fast_ok && impl != PDB_IMPL_GENERIC) {
@@ -316,7 +411,11 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
     p.counters = reinterpret_cast<unsigned long long*>(wb + ws.counters_off);
     p.partials = reinterpret_cast<float*>(wb + ws.partials_off);
     p.epoch = next_epoch();
-    fk.launch(p, (int)grid, fk.smem((int)B), st);
+    CUtensorMap kmap, vmap;
+    if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
+                    encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
+      return fail(PDB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV pools");
+    fk.launch(p, (int)grid, fk.smem((int)B), st, &kmap, &vmap);
   } else {
     const int splits = generic_splits(max_length);
     const size_t need = generic_ws(B, H, D, splits);

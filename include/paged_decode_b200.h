@@ -55,10 +55,12 @@ typedef enum {
 /* Kernel selection for pdb_paged_attention_impl. */
 typedef enum {
   PDB_IMPL_AUTO = 0,    /* stream-K kernel when the shape allows, else generic  */
-  PDB_IMPL_FAST = 1,    /* stream-K, GQA-shared tiles: tensor cores for FP16
-                           head_dim 64/128, SIMT otherwise                     */
+  PDB_IMPL_FAST = 1,    /* stream-K, GQA-shared tiles: FP16 head_dim 64/128 on
+                           tensor cores (TMA-fed when block_size % 16 == 0),
+                           SIMT otherwise                                      */
   PDB_IMPL_GENERIC = 2, /* any head_dim <= 256 / any alignment, split + combine */
-  PDB_IMPL_SIMT = 3     /* stream-K with the SIMT inner loop only               */
+  PDB_IMPL_SIMT = 3,    /* stream-K with the SIMT inner loop only               */
+  PDB_IMPL_MMA = 4      /* stream-K, tensor cores fed by cp.async (no TMA)      */
 } pdb_impl_t;
 
 /* Bits of the per-device error word (pdb_read_device_errors). */
@@ -66,6 +68,8 @@ typedef enum {
 #define PDB_DEVERR_LENGTH 0x2u       /* length < 0 or > table_width*block_size   */
 #define PDB_DEVERR_SLOT 0x4u         /* KV slot outside the pool                  */
 #define PDB_DEVERR_VALID_COUNT 0x8u  /* valid-row count != number of slots        */
+#define PDB_DEVERR_TIMEOUT 0x10u     /* a bounded wait on a shared-memory barrier
+                                        expired (never expected; see kernel notes) */
 
 /* Thread-local message of the last failed call ("" if none). */
 PDB_API const char* pdb_last_error(void);

@@ -17,8 +17,8 @@ pytestmark = pytest.mark.gpu
 mg = golden_module()
 W = import_module("workloads")
 _lib = import_module("_lib")
-IMPLS = [_lib.IMPL_AUTO, _lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT]
-STREAMK = (_lib.IMPL_FAST, _lib.IMPL_SIMT)
+IMPLS = [_lib.IMPL_AUTO, _lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT, _lib.IMPL_MMA]
+STREAMK = (_lib.IMPL_FAST, _lib.IMPL_SIMT, _lib.IMPL_MMA)
 
 
 def gold(name):
@@ -85,7 +85,7 @@ def test_stale_pool_bytes_are_never_read(pkg, cuda, dtype, impl):
     assert torch.equal(clean, poisoned)
 
 
-@pytest.mark.parametrize("impl", [_lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT])
+@pytest.mark.parametrize("impl", [_lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT, _lib.IMPL_MMA])
 def test_repeated_calls_are_deterministic(pkg, cuda, impl):
     w = W.llama3_8b(batch=24, layers=1)
     t = W.materialize(w, cuda)
@@ -108,17 +108,20 @@ def test_smollm_fp16_layer(pkg, cuda):
 
 
 def test_llama3_full_batch(pkg, cuda):
-    """Llama-3-8B shape at the full batch of 256, one layer: the three kernels
-    (tensor-core stream-K, SIMT stream-K, generic split) agree everywhere, and
-    12 sequences (shortest, longest, random) match the CPU oracle."""
+    """Llama-3-8B shape at the full batch of 256, one layer: the four kernels
+    (TMA-fed and cp.async-fed tensor-core stream-K, SIMT stream-K, generic
+    split) agree everywhere, and 12 sequences (shortest, longest, random)
+    match the CPU oracle."""
     w = W.llama3_8b(layers=1)
     t = W.materialize(w, cuda)
     args = (t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths, w.max_length)
     fast = pkg.paged_attention(*args, impl=_lib.IMPL_FAST)
     generic = pkg.paged_attention(*args, impl=_lib.IMPL_GENERIC)
     simt = pkg.paged_attention(*args, impl=_lib.IMPL_SIMT)
-    assert_parity(fast, generic.cpu(), "tensor-core vs generic")
+    mma = pkg.paged_attention(*args, impl=_lib.IMPL_MMA)
+    assert_parity(fast, generic.cpu(), "tma tensor-core vs generic")
     assert_parity(simt, generic.cpu(), "simt vs generic")
+    assert_parity(mma, generic.cpu(), "cp.async tensor-core vs generic")
     order = torch.argsort(w.lengths)
     pick = torch.cat([order[:3], order[-3:], torch.randperm(w.batch, generator=torch.Generator().manual_seed(0))[:6]])
     pick = pick.unique()
