@@ -362,7 +362,7 @@ def run_ours(args):
     peak = peak or 6650.0
     achieved = attn_bytes / (ms_attn * 1e-3) / 1e9
     traffic = None
-    tf = REPO / "profiles" / "traffic.json"
+    tf = REPO / "profiles" / "traffic_attn_tma_llama3_b256.json"
     if tf.exists():
         tj = json.loads(tf.read_text())
         if tj.get("workload") == full.name and tj.get("world") == world:
