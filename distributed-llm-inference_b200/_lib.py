@@ -28,6 +28,9 @@ SIGNATURES = {
     "pdb_paged_attention_impl": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
                                           _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                           _c_i64, _c_i64, _c_int, _c_ptr, _c_size, _c_ptr, _c_int]),
+    "pdb_paged_attention_noalloc": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                             _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                             _c_i64, _c_i64, _c_i64, _c_int, _c_ptr]),
     "pdb_rope_kv_write": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
                                    _c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_i64,
                                    _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,

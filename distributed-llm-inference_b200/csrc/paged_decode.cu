@@ -313,6 +313,31 @@ int current_device(int* dev) {
   return PDB_OK;
 }
 
+// ---- fixed scratch for callers that cannot allocate ------------------------
+// Used only by pdb_paged_attention_noalloc. The array lives in this file, so
+// every GPU that loads the library holds these bytes until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on device `dev` (which must be current).
+// In host code the symbol is only a handle; the address comes from the
+// runtime, once per device.
+int noalloc_scratch(int dev, unsigned char** out) {
+  static std::map<int, unsigned char*> cache;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) {
+    *out = it->second;
+    return PDB_OK;
+  }
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+  cache[dev] = static_cast<unsigned char*>(ptr);
+  *out = static_cast<unsigned char*>(ptr);
+  return PDB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -436,6 +461,61 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "paged_attention launch");
+  return PDB_OK;
+}
+
+int pdb_paged_attention_noalloc(const void* q, const void* k_pool, const void* v_pool,
+                                const int32_t* tables, const int32_t* lengths, void* out,
+                                int64_t B, int64_t H, int64_t D, int64_t N, int64_t bs,
+                                int64_t KVH, int64_t Dk, int64_t W, int64_t max_length,
+                                int dtype, void* stream) {
+  int rc = check_attention_args(B, H, D, N, bs, KVH, Dk, W, max_length, dtype);
+  if (rc) return rc;
+  if (!q || !k_pool || !v_pool || !tables || !lengths || !out)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  int dev = 0;
+  if ((rc = current_device(&dev))) return rc;
+  FastKernel fk;
+  if (!(fast_applicable(B, H, KVH, D, dtype, &fk, kAny, bs, N) && aligned16(q) &&
+        aligned16(k_pool) && aligned16(v_pool)))
+    return fail(PDB_ERR_INVALID_ARGUMENT,
+                "pdb_paged_attention_noalloc: shape or alignment needs the generic kernel; "
+                "use pdb_paged_attention with a workspace");
+  const int64_t grid = fast_grid(dev, fk, B, KVH, max_length);
+  if (grid <= 0) return fail(PDB_ERR_CUDA, "fast kernel cannot be resident on this device");
+  const FastWs ws = fast_ws_layout(B, KVH, D, fk.gp, grid);
+  if (ws.total > kNoAllocScratchBytes)
+    return fail(PDB_ERR_WORKSPACE,
+                "pdb_paged_attention_noalloc: this shape needs " + std::to_string(ws.total) +
+                    " bytes of scratch, above the fixed maximum of " +
+                    std::to_string(kNoAllocScratchBytes) + " bytes");
+  unsigned char* scratch = nullptr;
+  if ((rc = noalloc_scratch(dev, &scratch))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  pdb::AttnParams p{};
+  p.q = q; p.k_pool = k_pool; p.v_pool = v_pool;
+  p.tables = tables; p.lengths = lengths; p.out = out;
+  p.B = (int)B; p.H = (int)H; p.KVH = (int)KVH; p.G = (int)(H / KVH); p.D = (int)D;
+  p.num_blocks = N; p.block_size = (int)bs;
+  p.bs_shift = ((bs & (bs - 1)) == 0) ? __builtin_ctzll((unsigned long long)bs) : -1;
+  p.table_width = (int)W;
+  p.max_length = (int)max_length;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
+  p.counters = reinterpret_cast<unsigned long long*>(scratch + ws.counters_off);
+  p.partials = reinterpret_cast<float*>(scratch + ws.partials_off);
+  p.epoch = next_epoch();
+  // The shared array keeps the previous call's bytes: the arrival counters
+  // must read zero for this call (stream-ordered clear, nothing allocated).
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, (size_t)(B * KVH) * sizeof(unsigned long long), st);
+  if (e != cudaSuccess) return cuda_fail(e, "clear no-allocation scratch");
+  CUtensorMap kmap, vmap;
+  if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
+                  encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
+    return fail(PDB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV pools");
+  fk.launch(p, (int)grid, fk.smem((int)B), st, &kmap, &vmap);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_noalloc launch");
   return PDB_OK;
 }
 

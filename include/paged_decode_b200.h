@@ -123,6 +123,36 @@ PDB_API int pdb_paged_attention_impl(const void* q, const void* k_pool,
                              size_t workspace_bytes, void* stream, int impl);
 
 /*
+ * Paged GQA decode attention that allocates nothing and takes no workspace.
+ * No counterpart in the reference (its extension allocates through PyTorch).
+ * For callers that cannot allocate device memory or hand the library a
+ * buffer: a plugin hosted by an engine that owns the whole device-memory
+ * budget and gives plugins no allocator, or a loop that must not call
+ * cudaMalloc/cudaFree (cudaFree synchronises the device). Same arguments,
+ * checks and result as pdb_paged_attention, minus the workspace.
+ *   - Scratch is a fixed 2 MiB array inside the library on each GPU that
+ *     loads it (held until the process exits). Shapes whose scratch would
+ *     exceed it, or that only the generic kernel handles, are rejected with
+ *     PDB_ERR_WORKSPACE / PDB_ERR_INVALID_ARGUMENT and a message; for the
+ *     Llama-3-8B shape at batch 256 the need is about 1.3 MB.
+ *   - The first call on a device looks up that device's copy of the array
+ *     (the device must be current); make that first call before any stream
+ *     capture on the device.
+ *   - Every call on a device shares the one array: calls whose kernels can
+ *     overlap on the GPU (different streams without ordering) race and give
+ *     wrong results. Each call clears the part that must start at zero.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library call.
+ */
+PDB_API int pdb_paged_attention_noalloc(const void* q, const void* k_pool,
+                                        const void* v_pool, const int32_t* tables,
+                                        const int32_t* lengths, void* out,
+                                        int64_t batch, int64_t heads, int64_t head_dim,
+                                        int64_t num_blocks, int64_t block_size,
+                                        int64_t kv_heads, int64_t kv_head_dim,
+                                        int64_t table_width, int64_t max_length,
+                                        int dtype, void* stream);
+
+/*
  * Fused RoPE + paged KV-slot write (the prologue of one attention layer).
  * Replaces: PagedLlama.rope (worker/llama.py:108-117) followed by
  *           keys[layer][slots] = k ; values[layer][slots] = v
