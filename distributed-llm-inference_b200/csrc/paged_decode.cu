@@ -578,11 +578,26 @@ int pdb_rope_kv_write(const void* q, const void* k, const void* v, void* q_out, 
   p.slot_of_row = slot_of_row; p.num_slots = num_slots; p.seq = seq;
   p.heads = (int)heads; p.kv_heads = (int)kv_heads; p.dim = (int)head_dim;
   p.num_blocks = num_blocks; p.block_size = (int)block_size;
-  const size_t smem = (size_t)head_dim * sizeof(float);
-  if (dtype == PDB_DTYPE_FLOAT16)
-    pdb::rope_kv_write_kernel<__half><<<(unsigned)rows, 128, smem, st>>>(p);
-  else
-    pdb::rope_kv_write_kernel<float><<<(unsigned)rows, 128, smem, st>>>(p);
+  p.num_rows = rows;
+  const int esize = dtype == PDB_DTYPE_FLOAT16 ? 2 : 4;
+  const bool vec_ok = (head_dim * esize) % 32 == 0 && aligned16(q) && aligned16(k) &&
+                      aligned16(v) && aligned16(q_out) && aligned16(k_out) &&
+                      aligned16(k_pool) && aligned16(v_pool);
+  if (vec_ok) {
+    constexpr int kRows = 2;
+    const unsigned grid = (unsigned)((rows + kRows - 1) / kRows);
+    const size_t smem = (size_t)kRows * head_dim * sizeof(float);
+    if (dtype == PDB_DTYPE_FLOAT16)
+      pdb::rope_kv_write_vec_kernel<__half, kRows><<<grid, 256, smem, st>>>(p);
+    else
+      pdb::rope_kv_write_vec_kernel<float, kRows><<<grid, 256, smem, st>>>(p);
+  } else {
+    const size_t smem = (size_t)head_dim * sizeof(float);
+    if (dtype == PDB_DTYPE_FLOAT16)
+      pdb::rope_kv_write_kernel<__half><<<(unsigned)rows, 128, smem, st>>>(p);
+    else
+      pdb::rope_kv_write_kernel<float><<<(unsigned)rows, 128, smem, st>>>(p);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "rope_kv_write launch");
   return PDB_OK;

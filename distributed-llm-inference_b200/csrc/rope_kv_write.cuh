@@ -14,8 +14,7 @@
 //   out[j] = round(a - b);   out[j + D/2] = round(round(x[j+D/2]*c) + round(x[j]*s))
 // For FP16 each product/sum is formed exactly in fp32 and rounded once to
 // FP16 (an fp32 sum of two FP16 values rounds to the same FP16 value as an
-// exact sum: 24 >= 2*11+2 bits). cos/sin are evaluated in double precision and
-// rounded to fp32, i.e. correctly rounded.
+// exact sum: 24 >= 2*11+2 bits). cos/sin: see rope_cos_sin.
 #pragma once
 
 #include "common.cuh"
@@ -95,7 +94,28 @@ struct RopeParams {
   int heads, kv_heads, dim;
   int64_t num_blocks;
   int block_size;
+  int64_t num_rows;
 };
+
+// cos and sin of an fp32 angle, as fp32 values destined for dtype T.
+// sincosf is within 2 fp32 ulps. For FP16 the result is then rounded to 11
+// bits; when either value lies within 2 ulps of an FP16 rounding boundary
+// (rare) it is recomputed in double precision and rounded once to fp32, so
+// the FP16 values equal those of correctly rounded fp32 cos/sin.
+template <typename T>
+__device__ __forceinline__ void rope_cos_sin(float ang, float* c, float* s) {
+  sincosf(ang, s, c);
+  if constexpr (sizeof(T) == 2) {
+    auto near_boundary = [](float x) {
+      const float d = fabsf(x) * 2.5e-7f + 1e-37f;
+      return __float2half_rn(x - d) != __float2half_rn(x + d);
+    };
+    if (near_boundary(*c) || near_boundary(*s)) {
+      *c = (float)cos((double)ang);
+      *s = (float)sin((double)ang);
+    }
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ void rope_pair(const T* in, T* out, int j, int half,
@@ -124,10 +144,10 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
   const float fpos = (float)pos;  // positions.float(): round-to-nearest
   for (int j = threadIdx.x; j < half; j += blockDim.x) {
     const float ang = __fmul_rn(fpos, p.inv_freq[j]);
-    const double da = (double)ang;
-    // correctly rounded fp32 cos/sin, then rounded to the model dtype
-    cs[j] = Elem<T>::to_f(Elem<T>::from_f((float)cos(da)));
-    cs[half + j] = Elem<T>::to_f(Elem<T>::from_f((float)sin(da)));
+    float c, s;
+    rope_cos_sin<T>(ang, &c, &s);
+    cs[j] = Elem<T>::to_f(Elem<T>::from_f(c));
+    cs[half + j] = Elem<T>::to_f(Elem<T>::from_f(s));
   }
   __syncthreads();
 
@@ -192,6 +212,104 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
   if (vslot) {
     const int n = p.kv_heads * p.dim;
     for (int i = threadIdx.x; i < n; i += blockDim.x) vslot[i] = v[i];
+  }
+}
+
+// Vectorised variant: 16-byte loads and stores. Requires head_dim*e to be a
+// multiple of 32 bytes (each half a whole number of 16-byte chunks) and
+// 16-byte aligned q/k/v/outputs/pools. ROWS rows per CTA; per row, thread t
+// owns chunk t of the row's (head, 16-byte column) grid and rotates the
+// matching chunks of both halves. Rounding is identical to rope_kv_write_kernel.
+template <typename T, int ROWS>
+__global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
+  constexpr int VEC = 16 / (int)sizeof(T);
+  extern __shared__ float cs[];  // [ROWS][2][dim/2]
+  __shared__ long long slot_base[ROWS];
+  const int half = p.dim >> 1;
+  const int hchunks = half / VEC;  // chunks per half-row of one head
+  const int64_t r0 = (int64_t)blockIdx.x * ROWS;
+
+  for (int i = threadIdx.x; i < ROWS * half; i += blockDim.x) {
+    const int rr = i / half, j = i - rr * half;
+    const int64_t r = r0 + rr;
+    if (r >= p.num_rows) continue;
+    const int64_t bi = r / p.seq, si = r - bi * p.seq;
+    const float fpos = (float)p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
+    float c, s;
+    rope_cos_sin<T>(__fmul_rn(fpos, p.inv_freq[j]), &c, &s);
+    cs[(rr * 2) * half + j] = Elem<T>::to_f(Elem<T>::from_f(c));
+    cs[(rr * 2 + 1) * half + j] = Elem<T>::to_f(Elem<T>::from_f(s));
+  }
+  if (threadIdx.x < ROWS) {
+    const int64_t r = r0 + threadIdx.x;
+    long long base = -1;
+    if (r < p.num_rows) {
+      const int64_t slot = p.slot_of_row ? (int64_t)p.slot_of_row[r] : r;
+      if (slot >= 0) {
+        if (slot < p.num_slots) {
+          const int64_t phys = p.physical[slot], off = p.offsets[slot];
+          if (phys < 0 || phys >= p.num_blocks || off < 0 || off >= p.block_size) {
+            raise_error(0x4u);
+          } else {
+            base = (phys * p.block_size + off) * p.kv_heads * p.dim;
+          }
+        } else {
+          raise_error(0x8u);
+        }
+      }
+    }
+    slot_base[threadIdx.x] = base;
+  }
+  __syncthreads();
+
+  // Work items per row: q and k chunk pairs (one chunk of each half), then
+  // the v row copied as 2*kchunks plain chunks.
+  const int qchunks = p.heads * hchunks, kchunks = p.kv_heads * hchunks;
+  const int per_row = qchunks + kchunks + 2 * kchunks;
+  for (int i = threadIdx.x; i < ROWS * per_row; i += blockDim.x) {
+    const int rr = i / per_row, w = i - rr * per_row;
+    const int64_t r = r0 + rr;
+    if (r >= p.num_rows) continue;
+    const float* cr = cs + (rr * 2) * half;
+    const float* sr = cr + half;
+    if (w < qchunks + kchunks) {
+      const bool isq = w < qchunks;
+      const int ww = isq ? w : w - qchunks;
+      const int h = ww / hchunks, c = ww - h * hchunks;
+      const int nh = isq ? p.heads : p.kv_heads;
+      const T* in = static_cast<const T*>(isq ? p.q : p.k) + (r * nh + h) * p.dim;
+      T* out = static_cast<T*>(isq ? p.q_out : p.k_out) + (r * nh + h) * p.dim;
+      const int j0 = c * VEC;
+      float x1[VEC], x2[VEC];
+      Chunk<T>::to_f(*reinterpret_cast<const uint4*>(in + j0), x1);
+      Chunk<T>::to_f(*reinterpret_cast<const uint4*>(in + half + j0), x2);
+      uint4 o1, o2;
+      T* t1 = reinterpret_cast<T*>(&o1);
+      T* t2 = reinterpret_cast<T*>(&o2);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float cc = cr[j0 + e], ss = sr[j0 + e];
+        const T a = Elem<T>::from_f(__fmul_rn(x1[e], cc));
+        const T b = Elem<T>::from_f(__fmul_rn(x2[e], ss));
+        const T d = Elem<T>::from_f(__fmul_rn(x2[e], cc));
+        const T f = Elem<T>::from_f(__fmul_rn(x1[e], ss));
+        t1[e] = Elem<T>::from_f(__fsub_rn(Elem<T>::to_f(a), Elem<T>::to_f(b)));
+        t2[e] = Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(d), Elem<T>::to_f(f)));
+      }
+      *reinterpret_cast<uint4*>(out + j0) = o1;
+      *reinterpret_cast<uint4*>(out + half + j0) = o2;
+      if (!isq && slot_base[rr] >= 0) {
+        T* ks = static_cast<T*>(p.k_pool) + slot_base[rr] + h * p.dim;
+        *reinterpret_cast<uint4*>(ks + j0) = o1;
+        *reinterpret_cast<uint4*>(ks + half + j0) = o2;
+      }
+    } else if (slot_base[rr] >= 0) {
+      // v: copy the row's 2*kchunks 16-byte chunks to the slot unchanged
+      const int c = w - qchunks - kchunks;  // 0 .. 2*kchunks-1 over the full row
+      const T* vin = static_cast<const T*>(p.v) + r * p.kv_heads * p.dim;
+      T* vs = static_cast<T*>(p.v_pool) + slot_base[rr];
+      reinterpret_cast<uint4*>(vs)[c] = reinterpret_cast<const uint4*>(vin)[c];
+    }
   }
 }
 

@@ -140,3 +140,30 @@ def test_prologue_then_attention_llama3(pkg, cuda):
     lens = w.lengths[pick]
     ref = opa.paged_attention(qo.cpu()[pick], kp, vp, tabs, lens, int(lens.max()))
     assert_parity(out.cpu()[pick], ref, "llama3 pipeline")
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.float16, 40), (torch.float32, 36), (torch.float16, 64)])
+def test_rope_vector_and_scalar_paths(pkg, cuda, dtype, D):
+    """head_dim*e a multiple of 32 bytes takes the vectorised kernel, other even
+    head dims the scalar one; both match the oracle and write the same slots."""
+    g = torch.Generator().manual_seed(D)
+    B, H, KVH, N, bs = 5, 6, 2, 12, 8
+    q = (torch.randn(B, 1, H, D, generator=g) * 2).to(dtype)
+    k = (torch.randn(B, 1, KVH, D, generator=g) * 2).to(dtype)
+    v = torch.randn(B, 1, KVH, D, generator=g).to(dtype)
+    pos = torch.tensor([[0], [7], [8], [1000], [8191]], dtype=torch.int64)
+    phys = torch.tensor([3, 0, 11, 5, 7], dtype=torch.int64)
+    off = torch.tensor([0, 7, 3, 1, 6], dtype=torch.int64)
+    inv = W.inv_freq(1e4, D)
+    pool_k = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
+    pool_v = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
+    qr, kr = orope.rope(q, k, pos, inv)
+    kd, vd = pool_k.to(cuda), pool_v.to(cuda)
+    qo, ko = pkg.rope_kv_write(q.to(cuda), k.to(cuda), v.to(cuda), kd, vd, phys.to(cuda),
+                               off.to(cuda), pos.to(cuda), inv.to(cuda))
+    assert_parity(qo, qr, f"q D={D}")
+    assert_parity(ko, kr, f"k D={D}")
+    exp_k, exp_v = pool_k.clone(), pool_v.clone()
+    kv_cache.write_decode(exp_k, phys, off, ko.cpu()[:, 0])
+    kv_cache.write_decode(exp_v, phys, off, v[:, 0])
+    assert torch.equal(kd.cpu(), exp_k) and torch.equal(vd.cpu(), exp_v)
