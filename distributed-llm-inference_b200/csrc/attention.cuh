@@ -29,7 +29,7 @@
 //        read it there: K/V cross HBM exactly once.
 //      - A (sequence, kv head) segment cut by a CTA boundary is a "piece":
 //        its partial (m, l, o) goes to the workspace and the last CTA to
-//        finish a piece of that segment (epoch-tagged arrival counter, no
+//        finish a piece of that segment (one wrap-around atomic per piece, no
 //        waiting) merges the pieces and writes the output.
 //  * attn_generic_kernel + attn_combine_kernel — any head_dim <= 256, any
 //    group size, any alignment: grid (splits, heads, batch), one query head
@@ -57,9 +57,8 @@ struct AttnParams {
   int max_length;
   float scale_log2;  // log2(e) / sqrt(D)
   // workspace
-  unsigned long long* counters;  // stream-K: [B*KVH] epoch<<32 | arrivals
+  unsigned int* counters;        // stream-K: [B*KVH] arrivals, zero between calls
   float* partials;               // stream-K: [2*grid][GP*(D+2)]; generic: [B*H*splits][D+2]
-  uint32_t epoch;
   int splits;  // generic
   int chunk;   // generic: tokens per split
 };
@@ -109,6 +108,20 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Arrival on a segment's counter: returns the previous count and wraps the
+// counter to 0 when it reaches `last` (so it is zero again after the final
+// arrival). Release orders this CTA's partial stores (made visible to this
+// thread by the preceding barrier) before the count; acquire orders the
+// final arrival before its reads of the other pieces' partials.
+__device__ __forceinline__ unsigned arrive_wrap(unsigned* ctr, unsigned last) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;\n"
+               : "=r"(old)
+               : "l"(ctr), "r"(last)
+               : "memory");
+  return old;
 }
 
 // Byte offset of 16-byte chunk `col` of token row `row` in a staged tile.
@@ -642,55 +655,35 @@ __device__ __forceinline__ void finish_piece(const AttnParams& p, const Cursor& 
   }
 
   if (!whole) {
-    __threadfence();
-    sync();
+    sync();  // all partial stores of this CTA precede thread 0's release
     const int64_t S0 = cc.seg, S1 = cc.seg + cc.nu;
     const int64_t c0 = part_owner(S0, U, grid), c1 = part_owner(S1 - 1, U, grid);
-    unsigned long long* ctr = p.counters + ((int64_t)cc.b * p.KVH + cc.h);
     if (tid == 0) {
-      // Arrive: one CAS loop, bounded (each failure means another piece of
-      // this segment arrived, so at most pieces-1 retries are possible).
-      const unsigned long long ep = (unsigned long long)p.epoch << 32;
-      unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
-      int last = 0;
-      bool done = false;
-      for (int it = 0; it < (1 << 20) && !done; ++it) {
-        const unsigned cnt = ((old >> 32) == p.epoch) ? (unsigned)(old & 0xffffffffull) : 0u;
-        const unsigned long long nw = ep | (unsigned long long)(cnt + 1u);
-        const unsigned long long prev = atomicCAS(ctr, old, nw);
-        if (prev == old) {
-          done = true;
-          last = ((int64_t)cnt + 1 == c1 - c0 + 1) ? 1 : 0;
-        } else {
-          old = prev;
-        }
-      }
-      misc[1] = last;
+      const unsigned last = (unsigned)(c1 - c0);  // pieces - 1
+      misc[1] = arrive_wrap(p.counters + ((int64_t)cc.b * p.KVH + cc.h), last) == last;
     }
     sync();
     if (misc[1]) {
-      __threadfence();
+      // Only CTA c0 can hold its piece in slot 1 (it is the one CTA whose
+      // range starts before the segment); every later CTA starts inside it.
+      const int64_t first_slot = 2 * c0 + (part_begin(c0, U, grid) < S0 ? 1 : 0);
       for (int idx = tid; idx < GP * D; idx += NT) {
         const int g = idx / D, d = idx - g * D;
         if (g >= p.G) continue;
-        float M_ = -INFINITY;
+        float M_ = -INFINITY, L = 0.f, O = 0.f;
         for (int64_t c = c0; c <= c1; ++c) {
-          const float* sl = p.partials +
-              (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * SLOT_FLOATS;
-          M_ = fmaxf(M_, __ldcg(sl + g));
-        }
-        float L = 0.f, O = 0.f;
-        for (int64_t c = c0; c <= c1; ++c) {
-          const float* sl = p.partials +
-              (size_t)(2 * c + (part_begin(c, U, grid) >= S0 ? 0 : 1)) * SLOT_FLOATS;
-          const float mc = __ldcg(sl + g);
-          const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M_);
-          L = fmaf(__ldcg(sl + GP + g), f, L);
-          O = fmaf(__ldcg(sl + 2 * GP + g * D + d), f, O);
+          const float* sl = p.partials + (size_t)(c == c0 ? first_slot : 2 * c) * SLOT_FLOATS;
+          const float mc = __ldcg(sl + g), lc = __ldcg(sl + GP + g);
+          const float oc = __ldcg(sl + 2 * GP + g * D + d);
+          const float Mn = fmaxf(M_, mc);
+          const float a = (M_ == -INFINITY) ? 0.f : exp2f(M_ - Mn);
+          const float b = (mc == -INFINITY) ? 0.f : exp2f(mc - Mn);
+          L = fmaf(L, a, lc * b);
+          O = fmaf(O, a, oc * b);
+          M_ = Mn;
         }
         outp[g * D + d] = Elem<T>::from_f(O / L);
       }
-      if (tid == 0) atomicExch(ctr, (unsigned long long)p.epoch << 32);
     }
   }
   sync();

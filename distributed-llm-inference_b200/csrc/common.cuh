@@ -103,10 +103,15 @@ __device__ __forceinline__ void cp_async_wait() {
 // [begin(c), begin(c+1)); CTAs beyond part_grid own nothing.
 constexpr int kUnitTokens = 16;
 
-// CTAs that take part: min(launched, total units), so that with
-// begin(c) = c*total/grid every participating CTA owns at least one unit.
+// CTAs that take part: at most one per kMinUnitsPerCta units (a tiny batch is
+// not shredded into many small pieces per segment) and at most `launched`;
+// with begin(c) = c*total/grid every participating CTA owns >= 1 unit.
+constexpr int64_t kMinUnitsPerCta = 16;
 __host__ __device__ __forceinline__ int64_t part_grid(int64_t launched, int64_t total) {
-  return launched < total ? launched : total;
+  int64_t g = total / kMinUnitsPerCta;
+  if (g < 1) g = 1;
+  if (g > total) g = total;
+  return launched < g ? launched : g;
 }
 __host__ __device__ __forceinline__ int64_t part_begin(int64_t c, int64_t total,
                                                        int64_t grid) {

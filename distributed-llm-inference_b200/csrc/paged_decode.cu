@@ -77,12 +77,6 @@ int ctas_per_sm(int dev, const void* fn, size_t smem, int threads) {
   return n;
 }
 
-std::atomic<uint32_t> g_epoch{1};
-uint32_t next_epoch() {
-  uint32_t e = g_epoch.fetch_add(1);
-  if (e == 0) e = g_epoch.fetch_add(1);  // 0 marks never-used counters
-  return e;
-}
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -272,7 +266,7 @@ struct FastWs {
 FastWs fast_ws_layout(int64_t B, int64_t KVH, int64_t D, int gp, int64_t grid) {
   FastWs w;
   w.counters_off = 0;
-  w.partials_off = align256((size_t)(B * KVH) * sizeof(unsigned long long));
+  w.partials_off = align256((size_t)(B * KVH) * sizeof(unsigned int));
   w.total = w.partials_off + align256((size_t)(2 * grid) * gp * (D + 2) * sizeof(float));
   return w;
 }
@@ -433,9 +427,12 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
       return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) +
                                          " bytes");
     unsigned char* wb = static_cast<unsigned char*>(workspace);
-    p.counters = reinterpret_cast<unsigned long long*>(wb + ws.counters_off);
+    p.counters = reinterpret_cast<unsigned int*>(wb + ws.counters_off);
     p.partials = reinterpret_cast<float*>(wb + ws.partials_off);
-    p.epoch = next_epoch();
+    // Arrival counters start from zero in every call: the workspace may hold
+    // anything (another shape's partials, say). Stream-ordered, no allocation.
+    cudaError_t ze = cudaMemsetAsync(p.counters, 0, (size_t)(B * KVH) * sizeof(unsigned), st);
+    if (ze != cudaSuccess) return cuda_fail(ze, "clear arrival counters");
     CUtensorMap kmap, vmap;
     if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
                     encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
@@ -502,12 +499,11 @@ int pdb_paged_attention_noalloc(const void* q, const void* k_pool, const void* v
   p.table_width = (int)W;
   p.max_length = (int)max_length;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
-  p.counters = reinterpret_cast<unsigned long long*>(scratch + ws.counters_off);
+  p.counters = reinterpret_cast<unsigned int*>(scratch + ws.counters_off);
   p.partials = reinterpret_cast<float*>(scratch + ws.partials_off);
-  p.epoch = next_epoch();
   // The shared array keeps the previous call's bytes: the arrival counters
   // must read zero for this call (stream-ordered clear, nothing allocated).
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, (size_t)(B * KVH) * sizeof(unsigned long long), st);
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, (size_t)(B * KVH) * sizeof(unsigned int), st);
   if (e != cudaSuccess) return cuda_fail(e, "clear no-allocation scratch");
   CUtensorMap kmap, vmap;
   if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&

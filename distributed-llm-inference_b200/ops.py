@@ -29,9 +29,8 @@ def _check(cond: bool, msg: str) -> None:
 
 # --------------------------------------------------------------------------
 # Workspace cache: one grow-only buffer per (device, stream, op). Calls on one
-# stream are ordered, so calls of the same op can share it; the buffer is
-# zero-filled when (re)allocated and the attention kernel keeps its
-# epoch-tagged arrival counters valid across calls.
+# stream are ordered, so calls of the same op can share it; the buffer
+# never needs clearing (each call clears the counters it uses).
 # --------------------------------------------------------------------------
 _ws_lock = threading.Lock()
 _ws_cache: dict[tuple[int, int, str], torch.Tensor] = {}

@@ -79,9 +79,9 @@ PDB_API const char* pdb_version(void);
 
 /*
  * Bytes of device workspace that pdb_paged_attention needs for this shape on
- * the current device (0 is a valid answer). The workspace is scratch: its
- * contents need not be preserved between calls, but calls that overlap on the
- * GPU must not share one. It must be 256-byte aligned.
+ * the current device (0 is a valid answer). It must be 256-byte aligned; its
+ * contents do not matter (each call clears what it needs), so allocate it once
+ * and reuse it. Calls that overlap on the GPU must not share one.
  */
 PDB_API size_t pdb_paged_attention_workspace_size(int64_t batch, int64_t heads,
                                           int64_t kv_heads, int64_t head_dim,

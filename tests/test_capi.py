@@ -103,9 +103,9 @@ def test_partition_covers_units_once_and_balances(lib, seed):
     assert total == kvh * int(np.sum((lengths.astype(np.int64) + 15) // 16))
     assert r[0, 0] == 0 and r[-1, 1] == total
     assert np.all(r[1:, 0] == r[:-1, 1])             # contiguous, no gap, no overlap
-    working = min(grid, total)                       # CTAs beyond the unit count idle
+    working = min(grid, min(total, max(1, total // 16)))  # >= 16 units per working CTA
     sizes = r[:working, 1] - r[:working, 0]
-    assert total == 0 or sizes.min() >= 1            # every working CTA owns >= 1 unit
+    assert total == 0 or sizes.min() >= min(16, total // working)  # no shredding
     assert sizes.max() - sizes.min() <= 1            # equal shares of 16-token units
     assert np.all(r[working:, 0] == r[working:, 1])
 
@@ -115,7 +115,7 @@ def test_partition_owner_formula(lib):
     lengths = [37, 0, 1000, 16, 17, 5000]
     for grid in (1, 3, 7, 148, 592, 5000):
         total, r = partition(lib, lengths, 8, grid)
-        g = min(grid, total)
+        g = min(grid, min(total, max(1, total // 16)))
         for u in range(0, total, max(1, total // 97)):
             owner = ((u + 1) * g + total - 1) // total - 1
             assert r[owner, 0] <= u < r[owner, 1]

@@ -60,15 +60,16 @@ def test_matches_workspace_entry_point_on_consecutive_calls(pkg, cuda, name):
 
 
 def test_rejects_shapes_beyond_the_fixed_scratch(pkg, cuda):
-    # 4096 sequences x 64 kv heads: the per-(sequence, kv head) arrival
+    # 4096 sequences x 128 kv heads: the per-(sequence, kv head) arrival
     # counters alone fill the fixed array. Lengths are zero, so even a wrong
     # launch would read no pages.
-    B, H, KVH, D, bs = 4096, 64, 64, 64, 16
+    B, H, KVH, D, bs = 4096, 128, 128, 64, 16
     q = torch.zeros(B, H, D, dtype=torch.float16, device=cuda)
     k = torch.zeros(4, bs, KVH, D, dtype=torch.float16, device=cuda)
     tables = torch.zeros(B, 1, dtype=torch.int32, device=cuda)
     lengths = torch.zeros(B, dtype=torch.int32, device=cuda)
     out = torch.empty_like(q)
     rc = call_noalloc(q, k, k, tables, lengths, 16, out)
-    assert rc == 2, _lib.last_error()
+    torch.cuda.synchronize()
+    assert rc == 2, f"status {rc}: {_lib.last_error()}"
     assert "fixed maximum" in _lib.last_error()
