@@ -49,6 +49,10 @@ def parse():
     ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16"], default="llama3_8b")
     ap.add_argument("--batch", type=int, default=None, help="override the workload batch")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling)")
+    ap.add_argument("--sharding", choices=["balanced", "contiguous"], default="balanced",
+                    help="how sequences are split over ranks (both give every rank B/P)")
+    ap.add_argument("--no-alt", action="store_true",
+                    help="at N>1, skip the second measurement with the other sharding")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -320,7 +324,7 @@ def run_ours(args):
                                 device_id=device)
     PKG.load_library()
     full = make_workload(args)
-    w = full.shard(rank, world) if world > 1 else full
+    w = full.shard(rank, world, args.sharding) if world > 1 else full
     t = W.materialize(w, device)
     step = DecodeStep(w, t)
     stream = torch.cuda.Stream(device)
@@ -379,6 +383,30 @@ def run_ours(args):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "path": "public ops with pinned host buffers, H2D/D2H on copy streams"}
 
+    # the other even split, measured the same way (N > 1 only)
+    alt = None
+    if world > 1 and not args.no_alt:
+        alt_mode = "contiguous" if args.sharding == "balanced" else "balanced"
+        del g_step, g_attn, g_pro
+        wa = full.shard(rank, world, alt_mode)
+        ta = W.materialize(wa, device)
+        step_a = DecodeStep(wa, ta)
+        with torch.cuda.stream(stream):
+            step_a()
+        torch.cuda.synchronize(device)
+        g_alt = capture(step_a, stream)
+        for _ in range(args.warmup):
+            with torch.cuda.stream(stream):
+                g_alt.replay()
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        ms_alt = max_over_ranks(time_graph(g_alt, args.steps, stream), world, device) / args.steps
+        barrier(world, device)
+        alt = {"sharding": alt_mode, "value": full.batch / (ms_alt * 1e-3), "ms_per_step": ms_alt,
+               "max_rank_tokens": max_over_ranks(float(wa.lengths.sum()), world, device)}
+        del g_alt, step_a, ta
+        g_step = g_attn = g_pro = None
+
     # output checksum across ranks (outside every timed region)
     chk = torch.tensor([float(sum(o.float().abs().sum() for o in step.out))], device=device,
                        dtype=torch.float64)
@@ -386,6 +414,7 @@ def run_ours(args):
         import torch.distributed as dist
         dist.all_reduce(chk)
 
+    max_rank_tokens = max_over_ranks(float(w.lengths.sum()), world, device)
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = cpu_baseline(w, t)
@@ -403,7 +432,12 @@ def run_ours(args):
                             if args.workload == "llama3_8b" else full.name,
                 "batch": full.batch, "layers": full.layers, "max_length": full.max_length,
                 "mean_length": float(full.lengths.float().mean()),
-                "sharding": "sequences split evenly over ranks; each rank owns its pools",
+                "sharding": (f"{args.sharding}: every rank owns B/P whole sequences and its own "
+                             "pools/tables" + ("; balanced = dealt longest-first to the rank with "
+                                               "the fewest KV tokens" if args.sharding == "balanced"
+                                               else "; contiguous = sequences [r*B/P, (r+1)*B/P)")),
+                "max_rank_tokens": max_rank_tokens,
+                "mean_rank_tokens": float(full.lengths.sum()) / world,
                 "l2": "inputs larger than L2 (KV pools %.1f GB per rank)" % (
                     2 * w.layers * w.num_blocks * w.block_size * w.kv_heads * w.head_dim
                     * w.elem_bytes / 1e9),
@@ -420,10 +454,11 @@ def run_ours(args):
             "gpu_launches": args.steps * w.layers * 2,
             "e2e": e2e,
             "cpu_baseline": base,
+            "alt_sharding": alt,
             "checksum": float(chk.item()),
         }
         print(json.dumps(line), flush=True)
-    del g_step, g_attn, g_pro
+    g_step = g_attn = g_pro = None
     if world > 1:
         import torch.distributed as dist
         dist.barrier(device_ids=[device.index])

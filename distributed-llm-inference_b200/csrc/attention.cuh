@@ -29,7 +29,7 @@
 //        read it there: K/V cross HBM exactly once.
 //      - A (sequence, kv head) segment cut by a CTA boundary is a "piece":
 //        its partial (m, l, o) goes to the workspace and the last CTA to
-//        finish a piece of that segment (one wrap-around atomic per piece, no
+//        finish a piece of that segment (a tagged arrival counter, no
 //        waiting) merges the pieces and writes the output.
 //  * attn_generic_kernel + attn_combine_kernel — any head_dim <= 256, any
 //    group size, any alignment: grid (splits, heads, batch), one query head
@@ -57,8 +57,9 @@ struct AttnParams {
   int max_length;
   float scale_log2;  // log2(e) / sqrt(D)
   // workspace
-  unsigned int* counters;        // stream-K: [B*KVH] arrivals, zero between calls
+  unsigned long long* counters;  // stream-K: [B*KVH] call tag << 16 | arrivals
   float* partials;               // stream-K: [2*grid][GP*(D+2)]; generic: [B*H*splits][D+2]
+  unsigned long long call_tag;   // 48-bit salted tag of this call
   int splits;  // generic
   int chunk;   // generic: tokens per split
 };
@@ -110,18 +111,39 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Arrival on a segment's counter: returns the previous count and wraps the
-// counter to 0 when it reaches `last` (so it is zero again after the final
-// arrival). Release orders this CTA's partial stores (made visible to this
-// thread by the preceding barrier) before the count; acquire orders the
-// final arrival before its reads of the other pieces' partials.
-__device__ __forceinline__ unsigned arrive_wrap(unsigned* ctr, unsigned last) {
-  unsigned old;
-  asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;\n"
-               : "=r"(old)
-               : "l"(ctr), "r"(last)
+// Arrival of one piece on its segment's counter. A counter word holds
+// (call tag << 16 | arrivals); a word carrying another call's tag (or any
+// stale bytes) counts as zero arrivals, so the workspace needs no clearing.
+// Returns true for the arrival that completes `pieces`; that arrival resets
+// the count (tag kept, so a replay of the same call finds zero). acq_rel:
+// the release orders this CTA's partial stores (made visible to this thread
+// by the preceding barrier) before the arrival, the acquire of the final
+// arrival orders its reads of the other pieces. The CAS loop is bounded:
+// each failure means another piece of this segment arrived.
+__device__ __forceinline__ unsigned long long cas_acq_rel(unsigned long long* p,
+                                                          unsigned long long cmp,
+                                                          unsigned long long val) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.cas.b64 %0, [%1], %2, %3;\n"
+               : "=l"(old)
+               : "l"(p), "l"(cmp), "l"(val)
                : "memory");
   return old;
+}
+__device__ __forceinline__ bool arrive_piece(unsigned long long* ctr, unsigned long long tag,
+                                             unsigned pieces) {
+  const unsigned long long hi = tag << 16;
+  unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
+  for (unsigned it = 0; it <= pieces + 64; ++it) {
+    const unsigned cnt = ((old >> 16) == tag) ? (unsigned)(old & 0xffffu) : 0u;
+    const bool last = cnt + 1 >= pieces;
+    const unsigned long long nw = hi | (last ? 0ull : (unsigned long long)(cnt + 1));
+    const unsigned long long prev = cas_acq_rel(ctr, old, nw);
+    if (prev == old) return last;
+    old = prev;
+  }
+  raise_error(0x20u);  // cannot happen: more retries than pieces
+  return false;
 }
 
 // Byte offset of 16-byte chunk `col` of token row `row` in a staged tile.
@@ -658,10 +680,9 @@ __device__ __forceinline__ void finish_piece(const AttnParams& p, const Cursor& 
     sync();  // all partial stores of this CTA precede thread 0's release
     const int64_t S0 = cc.seg, S1 = cc.seg + cc.nu;
     const int64_t c0 = part_owner(S0, U, grid), c1 = part_owner(S1 - 1, U, grid);
-    if (tid == 0) {
-      const unsigned last = (unsigned)(c1 - c0);  // pieces - 1
-      misc[1] = arrive_wrap(p.counters + ((int64_t)cc.b * p.KVH + cc.h), last) == last;
-    }
+    if (tid == 0)
+      misc[1] = arrive_piece(p.counters + ((int64_t)cc.b * p.KVH + cc.h), p.call_tag,
+                             (unsigned)(c1 - c0 + 1));
     sync();
     if (misc[1]) {
       // Only CTA c0 can hold its piece in slot 1 (it is the one CTA whose

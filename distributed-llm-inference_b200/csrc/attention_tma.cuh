@@ -134,6 +134,11 @@ attn_tma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     }
     fence_barrier_init();
   }
+  launch_dependents();
+  // Launch, shared-memory set-up and barrier init overlap the end of the
+  // previous kernel in the stream; every global read or write comes after
+  // this wait (the previous kernel may write q, the pools, lengths, tables).
+  grid_dependency_wait();
   const int64_t U = plan_units<NT>(p, P, Ls, misc);  // ends with __syncthreads
 
   for (int b = blockIdx.x; b < p.B; b += gridDim.x) {

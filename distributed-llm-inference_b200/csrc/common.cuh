@@ -16,6 +16,20 @@ __device__ __forceinline__ void raise_error(unsigned bit) {
   atomicOr(&g_device_errors, bit);
 }
 
+// ---- programmatic dependent launch -----------------------------------------
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream is still running. It must call
+// grid_dependency_wait() before it reads what that kernel writes or writes
+// anything that kernel may touch; launch_dependents() lets the next kernel in
+// the stream start its own independent set-up early. Both are no-ops for a
+// kernel launched without the attribute.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" :::);
+}
+
 // ---- element conversion ---------------------------------------------------
 template <typename T> struct Elem;
 template <> struct Elem<float> {

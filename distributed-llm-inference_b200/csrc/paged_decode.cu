@@ -4,6 +4,7 @@
 // All kernels are compiled in this one translation unit (the headers below),
 // so the per-device error word is a single __device__ variable.
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -11,6 +12,7 @@
 #include <mutex>
 #include <string>
 #include <tuple>
+#include <utility>
 
 #include <cudaTypedefs.h>
 
@@ -80,6 +82,20 @@ int ctas_per_sm(int dev, const void* fn, size_t smem, int threads) {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// 48-bit tag per call: a process salt plus a call counter, so that counter
+// words left by other calls, processes or stale bytes do not match.
+unsigned long long next_call_tag() {
+  static std::atomic<unsigned long long> counter{0};
+  static const unsigned long long salt = [] {
+    unsigned long long x = (unsigned long long)std::chrono::high_resolution_clock::now()
+                               .time_since_epoch().count();
+    x ^= reinterpret_cast<uintptr_t>(&counter);
+    x ^= x >> 33; x *= 0xff51afd7ed558ccdull; x ^= x >> 33;  // splitmix-style mixing
+    return x;
+  }();
+  return (salt + 0x9e3779b97f4a7c15ull * (counter.fetch_add(1) + 1)) & ((1ull << 48) - 1);
+}
+
 // ---- stream-K kernel registry -----------------------------------------------
 struct FastKernel {
   const void* fn;
@@ -103,10 +119,30 @@ FastKernel make_fast() {
                     &launch_streamk<M>, &pdb::StreamK<M>::smem_bytes, M::GP, M::NT, false};
 }
 
+// Launch with programmatic stream serialization: the kernel may begin while
+// the previous kernel in the stream finishes (it waits on the device, with
+// griddepcontrol, before touching that kernel's outputs).
+template <typename... ExpT, typename... ActT>
+cudaError_t launch_pdl(void (*kernel)(ExpT...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, ActT&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<ActT>(args)...);
+}
+
 template <class M>
 void launch_tma(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st,
                 const CUtensorMap* kmap, const CUtensorMap* vmap) {
-  pdb::attn_tma_kernel<M><<<grid, pdb::TmaStreamK<M>::NT, smem, st>>>(p, *kmap, *vmap);
+  launch_pdl(pdb::attn_tma_kernel<M>, dim3(grid), dim3(pdb::TmaStreamK<M>::NT), smem, st, p,
+             *kmap, *vmap);
 }
 
 template <class M>
@@ -266,7 +302,7 @@ struct FastWs {
 FastWs fast_ws_layout(int64_t B, int64_t KVH, int64_t D, int gp, int64_t grid) {
   FastWs w;
   w.counters_off = 0;
-  w.partials_off = align256((size_t)(B * KVH) * sizeof(unsigned int));
+  w.partials_off = align256((size_t)(B * KVH) * sizeof(unsigned long long));
   w.total = w.partials_off + align256((size_t)(2 * grid) * gp * (D + 2) * sizeof(float));
   return w;
 }
@@ -427,12 +463,9 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
       return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) +
                                          " bytes");
     unsigned char* wb = static_cast<unsigned char*>(workspace);
-    p.counters = reinterpret_cast<unsigned int*>(wb + ws.counters_off);
+    p.counters = reinterpret_cast<unsigned long long*>(wb + ws.counters_off);
     p.partials = reinterpret_cast<float*>(wb + ws.partials_off);
-    // Arrival counters start from zero in every call: the workspace may hold
-    // anything (another shape's partials, say). Stream-ordered, no allocation.
-    cudaError_t ze = cudaMemsetAsync(p.counters, 0, (size_t)(B * KVH) * sizeof(unsigned), st);
-    if (ze != cudaSuccess) return cuda_fail(ze, "clear arrival counters");
+    p.call_tag = next_call_tag();
     CUtensorMap kmap, vmap;
     if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
                     encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
@@ -499,11 +532,12 @@ int pdb_paged_attention_noalloc(const void* q, const void* k_pool, const void* v
   p.table_width = (int)W;
   p.max_length = (int)max_length;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
-  p.counters = reinterpret_cast<unsigned int*>(scratch + ws.counters_off);
+  p.counters = reinterpret_cast<unsigned long long*>(scratch + ws.counters_off);
   p.partials = reinterpret_cast<float*>(scratch + ws.partials_off);
+  p.call_tag = next_call_tag();
   // The shared array keeps the previous call's bytes: the arrival counters
   // must read zero for this call (stream-ordered clear, nothing allocated).
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, (size_t)(B * KVH) * sizeof(unsigned int), st);
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, (size_t)(B * KVH) * sizeof(unsigned long long), st);
   if (e != cudaSuccess) return cuda_fail(e, "clear no-allocation scratch");
   CUtensorMap kmap, vmap;
   if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
@@ -584,9 +618,9 @@ int pdb_rope_kv_write(const void* q, const void* k, const void* v, void* q_out, 
     const unsigned grid = (unsigned)((rows + kRows - 1) / kRows);
     const size_t smem = (size_t)kRows * head_dim * sizeof(float);
     if (dtype == PDB_DTYPE_FLOAT16)
-      pdb::rope_kv_write_vec_kernel<__half, kRows><<<grid, 256, smem, st>>>(p);
+      launch_pdl(pdb::rope_kv_write_vec_kernel<__half, kRows>, dim3(grid), dim3(256), smem, st, p);
     else
-      pdb::rope_kv_write_vec_kernel<float, kRows><<<grid, 256, smem, st>>>(p);
+      launch_pdl(pdb::rope_kv_write_vec_kernel<float, kRows>, dim3(grid), dim3(256), smem, st, p);
   } else {
     const size_t smem = (size_t)head_dim * sizeof(float);
     if (dtype == PDB_DTYPE_FLOAT16)

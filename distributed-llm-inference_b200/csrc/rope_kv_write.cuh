@@ -27,6 +27,8 @@ template <int THREADS, int ITEMS>
 __global__ void __launch_bounds__(THREADS)
 valid_scan_kernel(const uint8_t* __restrict__ valid, int64_t rows,
                   int64_t num_slots, int32_t* __restrict__ slot_of_row) {
+  grid_dependency_wait();
+  launch_dependents();
   __shared__ int warp_sums[THREADS / 32];
   __shared__ int carry_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -136,6 +138,8 @@ __device__ __forceinline__ void rope_pair(const T* in, T* out, int j, int half,
 // memory (already rounded to the model dtype) and reused by all heads.
 template <typename T>
 __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
+  grid_dependency_wait();
+  launch_dependents();
   extern __shared__ float cs[];  // [2][dim/2]
   const int64_t r = blockIdx.x;
   const int half = p.dim >> 1;
@@ -222,6 +226,8 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
 // matching chunks of both halves. Rounding is identical to rope_kv_write_kernel.
 template <typename T, int ROWS>
 __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
+  grid_dependency_wait();  // inputs may come from the previous kernel
+  launch_dependents();     // the attention kernel may start its set-up
   constexpr int VEC = 16 / (int)sizeof(T);
   extern __shared__ float cs[];  // [ROWS][2][dim/2]
   __shared__ long long slot_base[ROWS];

@@ -1,10 +1,16 @@
 """Sequence sharding across GPUs (one process per GPU).
 
-The decode path partitions naturally: sequences are independent, so rank r
-owns sequences [r*B//P, (r+1)*B//P) together with its own KV pools, block
-tables and allocator, and the hot path needs no collective. torch.distributed
-is used only around the measured region: a barrier, the max over ranks of
-the device-timed duration, and a sum of output checksums.
+The decode path partitions naturally: sequences are independent, so each
+rank owns a set of whole sequences together with its own KV pools, block
+tables and allocator, and the hot path needs no collective. Two even splits
+(every rank gets B//P or B//P+1 sequences):
+  contiguous  rank r owns sequences [r*B//P, (r+1)*B//P);
+  balanced    the same counts, but sequences are dealt longest first to the
+              rank with the fewest KV tokens so far that still has room, so
+              every rank streams about the same KV bytes (decode time is
+              proportional to them).
+torch.distributed is used only around the measured region: a barrier, the
+max over ranks of the device-timed duration, and a sum of output checksums.
 """
 from __future__ import annotations
 
@@ -17,6 +23,33 @@ def shard_bounds(batch: int, world: int, rank: int) -> tuple[int, int]:
     if not 0 <= rank < world:
         raise ValueError("rank out of range")
     return rank * batch // world, (rank + 1) * batch // world
+
+
+def shard_counts(batch: int, world: int) -> list[int]:
+    return [shard_bounds(batch, world, r)[1] - shard_bounds(batch, world, r)[0]
+            for r in range(world)]
+
+
+def balanced_assignment(lengths, world: int) -> list[list[int]]:
+    """Equal-count, token-balanced split of sequence indices (each list sorted)."""
+    lens = [int(x) for x in lengths]
+    cap = shard_counts(len(lens), world)
+    load, owned = [0] * world, [[] for _ in range(world)]
+    for i in sorted(range(len(lens)), key=lambda i: (-lens[i], i)):
+        r = min((r for r in range(world) if len(owned[r]) < cap[r]), key=lambda r: (load[r], r))
+        owned[r].append(i)
+        load[r] += lens[i]
+    return [sorted(o) for o in owned]
+
+
+def shard_indices(lengths, world: int, rank: int, mode: str = "balanced") -> list[int]:
+    """Indices of the sequences rank `rank` owns under `mode`."""
+    if mode == "contiguous":
+        lo, hi = shard_bounds(len(lengths), world, rank)
+        return list(range(lo, hi))
+    if mode == "balanced":
+        return balanced_assignment(lengths, world)[rank]
+    raise ValueError(f"unknown sharding mode {mode!r}")
 
 
 def _reduce(value: float, op, device) -> float:

@@ -28,7 +28,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from .sharding import shard_bounds
+from .sharding import shard_indices
 
 
 @dataclass
@@ -101,23 +101,21 @@ class DecodeWorkload:
         """Per decode step, all layers: prologue + attention bytes."""
         return self.layers * (self.attention_bytes() + self.prologue_bytes())
 
-    def shard(self, rank: int, world: int) -> "DecodeWorkload":
-        """Sequences [rank*B//world, (rank+1)*B//world) with their own pool.
-
-        Each rank owns its KV pool and block tables; the shard's tables are
-        renumbered into a pool of the shard's own size.
-        """
-        lo, hi = shard_bounds(self.batch, world, rank)
-        lengths = self.lengths[lo:hi].clone()
+    def shard(self, rank: int, world: int, mode: str = "balanced") -> "DecodeWorkload":
+        """The sequences rank `rank` owns (sharding.shard_indices), with a pool
+        of the shard's own size: each rank owns its KV pool and block tables,
+        renumbered into that pool."""
+        idx = shard_indices(self.lengths, world, rank, mode)
+        lengths = self.lengths[torch.tensor(idx, dtype=torch.int64)].clone()
         sub = make_decode_tables(lengths, self.block_size, self.seed * 1000 + rank,
                                  self.meta.get("pool_factor", 1.25), None)
         return DecodeWorkload(
-            name=f"{self.name}[{lo}:{hi}]", batch=hi - lo, heads=self.heads,
+            name=f"{self.name}[{mode} {rank}/{world}]", batch=len(idx), heads=self.heads,
             kv_heads=self.kv_heads, head_dim=self.head_dim, layers=self.layers,
             block_size=self.block_size, dtype=self.dtype, theta=self.theta,
             seed=self.seed * 1000 + rank, lengths=lengths, tables=sub[0], num_blocks=sub[1],
             used_blocks=sub[2], stale_scale=self.stale_scale,
-            meta=dict(self.meta, shard=(rank, world, lo, hi)))
+            meta=dict(self.meta, shard=(rank, world, mode, idx)))
 
 
 def make_decode_tables(lengths: torch.Tensor, block_size: int, seed: int,

@@ -70,6 +70,8 @@ typedef enum {
 #define PDB_DEVERR_VALID_COUNT 0x8u  /* valid-row count != number of slots        */
 #define PDB_DEVERR_TIMEOUT 0x10u     /* a bounded wait on a shared-memory barrier
                                         expired (never expected; see kernel notes) */
+#define PDB_DEVERR_ARRIVAL 0x20u     /* a piece could not register its arrival
+                                        (never expected)                          */
 
 /* Thread-local message of the last failed call ("" if none). */
 PDB_API const char* pdb_last_error(void);

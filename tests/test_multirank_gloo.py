@@ -40,9 +40,9 @@ def _worker_shards(rank, world, port, out_dir):
     S = importlib.import_module("distributed-llm-inference_b200.sharding")
     from oracle import paged_attention as opa
     full = W.llama3_8b(batch=12, layers=1)
-    shard = full.shard(rank, world)
+    shard = full.shard(rank, world, "contiguous")
     lo, hi = S.shard_bounds(full.batch, world, rank)
-    assert (lo, hi) == shard.meta["shard"][2:]
+    assert shard.meta["shard"][3] == list(range(lo, hi))
     assert torch.equal(shard.lengths, full.lengths[lo:hi])
     t = W.materialize(shard, "cpu")
     out = opa.paged_attention(t.q[0], t.k_pools[0], t.v_pools[0], shard.tables, shard.lengths,
@@ -117,3 +117,26 @@ def test_shard_bounds_even():
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
             sizes = [h - l for l, h in spans]
             assert max(sizes) - min(sizes) <= 1
+
+
+def test_balanced_assignment_equal_counts_and_tokens():
+    sys.path.insert(0, str(REPO))
+    import importlib
+    S = importlib.import_module("distributed-llm-inference_b200.sharding")
+    W = importlib.import_module("distributed-llm-inference_b200.workloads")
+    lengths = W.llama3_8b().lengths
+    for P in (1, 2, 4, 8):
+        owned = S.balanced_assignment(lengths, P)
+        flat = sorted(i for o in owned for i in o)
+        assert flat == list(range(len(lengths)))             # every sequence exactly once
+        assert {len(o) for o in owned} == set(S.shard_counts(len(lengths), P))
+        loads = [int(lengths[o].sum()) for o in owned]
+        assert max(loads) / (sum(loads) / P) < 1.01           # token-balanced
+        contiguous = [int(lengths[S.shard_indices(lengths, P, r, "contiguous")].sum())
+                      for r in range(P)]
+        assert max(loads) <= max(contiguous)
+    w = W.llama3_8b(batch=16, layers=1)
+    shards = [w.shard(r, 4) for r in range(4)]
+    assert sorted(i for sh in shards for i in sh.meta["shard"][3]) == list(range(16))
+    for sh in shards:
+        assert torch.equal(sh.lengths, w.lengths[torch.tensor(sh.meta["shard"][3])])
