@@ -10,12 +10,12 @@ Public ops (drop-in for the reference's decode path):
 The package directory name contains '-', so import it with
 importlib.import_module("distributed-llm-inference_b200").
 """
-from ._lib import IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA, load as load_library  # noqa: F401
+from ._lib import IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA, IMPL_TMA_STATIC, load as load_library  # noqa: F401
 from .ops import fast_grid_size, paged_attention, read_device_errors, rope_kv_write  # noqa: F401
 from .integration import cuda_paged_attention, install  # noqa: F401
 
 __all__ = [
     "paged_attention", "rope_kv_write", "cuda_paged_attention", "install",
     "read_device_errors", "fast_grid_size", "load_library",
-    "IMPL_AUTO", "IMPL_FAST", "IMPL_GENERIC", "IMPL_SIMT", "IMPL_MMA",
+    "IMPL_AUTO", "IMPL_FAST", "IMPL_GENERIC", "IMPL_SIMT", "IMPL_MMA", "IMPL_TMA_STATIC",
 ]

@@ -38,12 +38,13 @@ SIGNATURES = {
     "pdb_rope_kv_write_workspace_size": (_c_size, [_c_i64, _c_i64, _c_int]),
     "pdb_read_device_errors": (_c_int, [ctypes.POINTER(ctypes.c_uint32), _c_int]),
     "pdb_debug_partition": (_c_i64, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr]),
+    "pdb_debug_dyn_partition": (_c_i64, [_c_i64, _c_i64, _c_ptr, _c_i64]),
     "pdb_fast_grid_size": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64, _c_int]),
 }
 
 DTYPE_FLOAT32 = 0
 DTYPE_FLOAT16 = 1
-IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA = 0, 1, 2, 3, 4
+IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA, IMPL_TMA_STATIC = 0, 1, 2, 3, 4, 5
 STATUS_NAMES = {0: "ok", 1: "invalid argument", 2: "workspace", 3: "cuda"}
 
 _lock = threading.Lock()

@@ -111,15 +111,6 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Arrival of one piece on its segment's counter. A counter word holds
-// (call tag << 16 | arrivals); a word carrying another call's tag (or any
-// stale bytes) counts as zero arrivals, so the workspace needs no clearing.
-// Returns true for the arrival that completes `pieces`; that arrival resets
-// the count (tag kept, so a replay of the same call finds zero). acq_rel:
-// the release orders this CTA's partial stores (made visible to this thread
-// by the preceding barrier) before the arrival, the acquire of the final
-// arrival orders its reads of the other pieces. The CAS loop is bounded:
-// each failure means another piece of this segment arrived.
 __device__ __forceinline__ unsigned long long cas_acq_rel(unsigned long long* p,
                                                           unsigned long long cmp,
                                                           unsigned long long val) {
@@ -130,20 +121,71 @@ __device__ __forceinline__ unsigned long long cas_acq_rel(unsigned long long* p,
                : "memory");
   return old;
 }
+__device__ __forceinline__ unsigned long long add_acq_rel(unsigned long long* p,
+                                                          unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;\n"
+               : "=l"(old)
+               : "l"(p), "l"(v)
+               : "memory");
+  return old;
+}
+__device__ __forceinline__ void store_relaxed(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+
+// Install this call's tag in a counter word of the form (tag << shift | count).
+// A word carrying another tag (an earlier call, or the stale bytes of a fresh
+// workspace) is replaced once by (tag << shift) with a compare-and-swap: the
+// first thread to try wins and every other CAS fails by returning the
+// installed word. Bounded: nothing else writes a stale word while a call runs.
+__device__ __forceinline__ bool install_tag(unsigned long long* ctr, unsigned long long tag,
+                                            int shift, int64_t bound) {
+  const unsigned long long hi = tag << shift;
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(ctr);
+  for (int64_t it = 0; (cur >> shift) != tag; ++it) {
+    if (it > bound) {
+      raise_error(0x20u);
+      return false;
+    }
+    const unsigned long long prev = cas_acq_rel(ctr, cur, hi);
+    cur = prev == cur ? hi : prev;
+  }
+  return true;
+}
+
+// Arrival of one piece on its segment's counter, a word (call tag << 16 |
+// arrivals): the tag is installed if stale, then each piece adds one. Returns
+// true for the arrival that completes `pieces`, which puts the count back to
+// zero (tag kept), so a CUDA-graph replay of the same call — same tag — starts
+// from zero; no other piece of the segment touches the word after it. acq_rel:
+// the release orders this CTA's partial stores (made visible to this thread
+// by the preceding barrier) before its arrival; the final arrival's acquire,
+// through the chain of read-modify-writes, orders its reads of every other
+// piece. One fetch-add per piece: the pieces of a segment that finish
+// together do not serialise on a CAS loop.
 __device__ __forceinline__ bool arrive_piece(unsigned long long* ctr, unsigned long long tag,
                                              unsigned pieces) {
-  const unsigned long long hi = tag << 16;
-  unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
-  for (unsigned it = 0; it <= pieces + 64; ++it) {
-    const unsigned cnt = ((old >> 16) == tag) ? (unsigned)(old & 0xffffu) : 0u;
-    const bool last = cnt + 1 >= pieces;
-    const unsigned long long nw = hi | (last ? 0ull : (unsigned long long)(cnt + 1));
-    const unsigned long long prev = cas_acq_rel(ctr, old, nw);
-    if (prev == old) return last;
-    old = prev;
+  if (!install_tag(ctr, tag, 16, (int64_t)pieces + 64)) return false;
+  const unsigned long long old = add_acq_rel(ctr, 1ull);
+  const bool last = (unsigned)(old & 0xffffu) + 1u >= pieces;
+  if (last) store_relaxed(ctr, tag << 16);
+  return last;
+}
+
+// Arrival on a counter whose tag this thread installed earlier with
+// install_tag (so no other tag can be in the word): one fetch-add, with the
+// return value, reset and ordering of arrive_piece.
+__device__ __forceinline__ bool arrive_installed(unsigned long long* ctr, unsigned long long tag,
+                                                 unsigned pieces) {
+  const unsigned long long old = add_acq_rel(ctr, 1ull);
+  if ((old >> 16) != tag) {  // cannot happen after install_tag
+    raise_error(0x20u);
+    return false;
   }
-  raise_error(0x20u);  // cannot happen: more retries than pieces
-  return false;
+  const bool last = (unsigned)(old & 0xffffu) + 1u >= pieces;
+  if (last) store_relaxed(ctr, tag << 16);
+  return last;
 }
 
 // Byte offset of 16-byte chunk `col` of token row `row` in a staged tile.
@@ -634,6 +676,97 @@ struct StreamK {
   }
 };
 
+// Combine the partial slots of pieces w_first..w_last of one segment (the
+// piece of w_first in `first_slot`, every later worker's in slot 2w) into the
+// segment's G output rows, rescaling in base 2 piece by piece. Called by NTH
+// threads, t in [0, NTH). When GP*D splits evenly, thread t owns the E
+// consecutive elements [t*E, (t+1)*E) of one row and loads the entries (and
+// the row's max and sum) of PU pieces at once — PU as large as the caller's
+// register budget BUDGET (floats in flight per thread) allows, at most 8 —
+// before combining them in piece order, so a merge costs about one L2 round
+// trip per PU pieces. Per element the arithmetic and its order are those of a
+// plain sequential loop over the pieces.
+template <class T, int GP, int D, int NTH, int BUDGET>
+__device__ __forceinline__ void merge_slots(const float* partials, T* outp, int G,
+                                            int64_t w_first, int64_t w_last,
+                                            int64_t first_slot, int t) {
+  constexpr int SLOT_FLOATS = GP * (D + 2);
+  constexpr int E = GP * D / NTH;
+  constexpr int E_DIV = E > 0 ? E : 1;
+  if constexpr (GP * D % NTH == 0 && E >= 1 && D % E_DIV == 0) {
+    constexpr int PU0 = BUDGET / (E + 2);
+    constexpr int PU = PU0 < 1 ? 1 : (PU0 > 8 ? 8 : PU0);  // pieces per batch of loads
+    // 16-byte loads when every thread's run of E floats starts 16-byte aligned
+    constexpr bool VEC = E % 4 == 0 && (SLOT_FLOATS * 4) % 16 == 0 && (2 * GP * 4) % 16 == 0 &&
+                         (D * 4) % 16 == 0;
+    const int g = t * E / D, d0 = t * E - g * D;
+    float Mx = -INFINITY, Lx = 0.f, Ox[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) Ox[e] = 0.f;
+    for (int64_t w0 = w_first; w0 <= w_last; w0 += PU) {
+      float mc[PU], lc[PU], oc[PU][E];
+#pragma unroll
+      for (int u = 0; u < PU; ++u) {
+        const int64_t w = w0 + u;
+        if (w <= w_last) {
+          const float* sl = partials + (size_t)(w == w_first ? first_slot : 2 * w) * SLOT_FLOATS;
+          mc[u] = __ldcg(sl + g);
+          lc[u] = __ldcg(sl + GP + g);
+          const float* src = sl + 2 * GP + g * D + d0;
+          if constexpr (VEC) {
+#pragma unroll
+            for (int e = 0; e < E; e += 4) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(src + e));
+              oc[u][e] = v.x;
+              oc[u][e + 1] = v.y;
+              oc[u][e + 2] = v.z;
+              oc[u][e + 3] = v.w;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < E; ++e) oc[u][e] = __ldcg(src + e);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < PU; ++u) {
+        if (w0 + u <= w_last) {
+          const float Mn = fmaxf(Mx, mc[u]);
+          const float a = (Mx == -INFINITY) ? 0.f : exp2f(Mx - Mn);
+          const float b = (mc[u] == -INFINITY) ? 0.f : exp2f(mc[u] - Mn);
+          Lx = fmaf(Lx, a, lc[u] * b);
+#pragma unroll
+          for (int e = 0; e < E; ++e) Ox[e] = fmaf(Ox[e], a, oc[u][e] * b);
+          Mx = Mn;
+        }
+      }
+    }
+    if (g < G) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) outp[g * D + d0 + e] = Elem<T>::from_f(Ox[e] / Lx);
+    }
+  } else {
+    for (int idx = t; idx < GP * D; idx += NTH) {
+      const int g = idx / D, d = idx - g * D;
+      if (g >= G) continue;
+      float M_ = -INFINITY, L = 0.f, O = 0.f;
+#pragma unroll 4  // slot loads of consecutive pieces in flight together
+      for (int64_t w = w_first; w <= w_last; ++w) {
+        const float* sl = partials + (size_t)(w == w_first ? first_slot : 2 * w) * SLOT_FLOATS;
+        const float mc = __ldcg(sl + g), lc = __ldcg(sl + GP + g);
+        const float oc = __ldcg(sl + 2 * GP + g * D + d);
+        const float Mn = fmaxf(M_, mc);
+        const float a = (M_ == -INFINITY) ? 0.f : exp2f(M_ - Mn);
+        const float b = (mc == -INFINITY) ? 0.f : exp2f(mc - Mn);
+        L = fmaf(L, a, lc * b);
+        O = fmaf(O, a, oc * b);
+        M_ = Mn;
+      }
+      outp[g * D + d] = Elem<T>::from_f(O / L);
+    }
+  }
+}
+
 // Merge the NW warp states of a finished piece [piece_u0, ...) of segment
 // (cc.b, cc.h) and write the output, or publish the piece's partial and, if
 // this CTA is the last to finish a piece of the segment, combine all pieces.
@@ -688,23 +821,7 @@ __device__ __forceinline__ void finish_piece(const AttnParams& p, const Cursor& 
       // Only CTA c0 can hold its piece in slot 1 (it is the one CTA whose
       // range starts before the segment); every later CTA starts inside it.
       const int64_t first_slot = 2 * c0 + (part_begin(c0, U, grid) < S0 ? 1 : 0);
-      for (int idx = tid; idx < GP * D; idx += NT) {
-        const int g = idx / D, d = idx - g * D;
-        if (g >= p.G) continue;
-        float M_ = -INFINITY, L = 0.f, O = 0.f;
-        for (int64_t c = c0; c <= c1; ++c) {
-          const float* sl = p.partials + (size_t)(c == c0 ? first_slot : 2 * c) * SLOT_FLOATS;
-          const float mc = __ldcg(sl + g), lc = __ldcg(sl + GP + g);
-          const float oc = __ldcg(sl + 2 * GP + g * D + d);
-          const float Mn = fmaxf(M_, mc);
-          const float a = (M_ == -INFINITY) ? 0.f : exp2f(M_ - Mn);
-          const float b = (mc == -INFINITY) ? 0.f : exp2f(mc - Mn);
-          L = fmaf(L, a, lc * b);
-          O = fmaf(O, a, oc * b);
-          M_ = Mn;
-        }
-        outp[g * D + d] = Elem<T>::from_f(O / L);
-      }
+      merge_slots<T, GP, D, NT, 16>(p.partials, outp, p.G, c0, c1, first_slot, tid);
     }
   }
   sync();

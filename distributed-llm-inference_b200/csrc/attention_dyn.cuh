@@ -1,0 +1,557 @@
+// Stream-K paged decode attention with a TMA producer warp and a dynamic tail
+// (sm_100a, FP16). Same math (MmaMath, tensor cores) and staging (3-D TMA
+// boxes, 128-byte swizzle) as attn_tma_kernel; what changes is the
+// schedule.
+//
+// CTAs that receive equal static shares do not finish together: measured on
+// B200, the last tile of equal shares lands up to ~15 % apart. So the unit
+// stream (16-token units ordered by sequence, kv head, token) is split into
+//   * a static head, the first 15/16 of the units, in one contiguous range
+//     per CTA (as in attn_tma_kernel), and
+//   * a tail, the last 1/16, cut into at most kTailChunksPerCta chunks per CTA
+//     of at least kMinChunkTiles 64-token tiles each, which CTAs claim one at
+//     a time with a tagged atomic counter once their static range is done.
+// Tail fraction and chunk size were chosen by measurement on B200 (Llama-3-8B
+// shape, batch 32 to 256): smaller chunks or a larger tail cost more in piece
+// finishes and merges than they gain in balance.
+// The unit stream lists first the sequences whose per-head segments are
+// longer than two tail chunks, then the others (each group in index order),
+// so the tail holds short segments that few chunk boundaries cut and the
+// merges at the end of the kernel combine few pieces.
+// Every range (a CTA's static range or a tail chunk) is a "worker" with a
+// contiguous unit range. A (sequence, kv head) segment cut by worker
+// boundaries is merged by the last of its pieces to arrive, exactly as in
+// attn_tma_kernel, with two partial slots per worker — so the workspace stays
+// bounded by the grid, not by the batch.
+//
+// The producer warp owns the schedule: it walks its workers, claims tail
+// chunks ahead of time, issues the TMA boxes and writes a per-stage record
+// (segment, token count, piece flags, merge information) that the four
+// tensor-core warps read after the stage's "full" barrier; a final record
+// marks the end. A piece that is not a whole segment costs the math warps
+// only its partial-slot stores: they queue the piece's arrival for an
+// epilogue warp and go on with the next tile, while the epilogue warp makes
+// the arrival (a gpu-scope release and an L2 round trip) and, for the last
+// piece of a segment, merges the segment's slots into its output rows. All
+// mbarrier waits and the claim loop are bounded.
+#pragma once
+
+#include "attention_tma.cuh"
+
+namespace pdb {
+
+constexpr int kTailDen = 16;         // tail = U / kTailDen units
+constexpr int kTailChunksPerCta = 4;  // target tail chunks per launched CTA
+constexpr int kMinChunkTiles = 4;     // a tail chunk covers at least this many tiles
+
+// Worker layout of one call: static workers 0..gs-1 over [0, Us), tail
+// workers gs..gs+K-1 over [Us, U).
+// begin(w) for w in [0, gs + K] is non-decreasing, begin(0) = 0,
+// begin(gs) = Us, begin(gs + K) = U; with U > 0, gs >= 1 and every worker
+// owns at least one unit (tail chunks at least kMinChunkTiles tiles).
+struct DynPlan {
+  int64_t U, Us, Ut, gs, K;
+  __host__ __device__ __forceinline__ int64_t begin(int64_t w) const {
+    // w == gs (end of the static region) stays in the first branch, so no
+    // division by K happens when there is no tail (K == 0).
+    return w <= gs ? part_begin(w, Us, gs) : Us + part_begin(w - gs, Ut, K);
+  }
+  __host__ __device__ __forceinline__ int64_t owner(int64_t u) const {
+    return u < Us ? part_owner(u, Us, gs) : gs + part_owner(u - Us, Ut, K);
+  }
+};
+
+__host__ __device__ __forceinline__ DynPlan make_dyn_plan(int64_t U, int64_t launched,
+                                                          int tile_units) {
+  DynPlan pl;
+  pl.U = U;
+  int64_t Ut = (U >= 8 * launched * tile_units) ? U / kTailDen : 0;
+  int64_t K = launched * kTailChunksPerCta;
+  const int64_t kmax = Ut / ((int64_t)kMinChunkTiles * tile_units);
+  if (K > kmax) K = kmax;
+  if (K <= 0) { K = 0; Ut = 0; }
+  pl.Ut = Ut;
+  pl.K = K;
+  pl.Us = U - Ut;
+  pl.gs = pl.Us > 0 ? part_grid(launched, pl.Us) : 0;
+  return pl;
+}
+
+__host__ __device__ __forceinline__ unsigned long long claim_tag(unsigned long long tag48) {
+  return tag48 & ((1ull << 44) - 1);  // 44 tag bits + 20 count bits per word
+}
+
+// Claim the next tail chunk from a counter word (call tag << 20 | claims):
+// the epilogue warp installs the call's tag when the CTA starts, so a claim
+// is normally one fetch-add (a claim that still finds another tag installs it
+// and claims again); the CTAs that finish their static ranges together do not
+// serialise on a CAS loop. With K > 0 every launched CTA claims until a claim comes back empty,
+// so a call makes exactly K + launched claims (far below 2^20); the last one
+// puts the count back to zero (tag kept), so a CUDA-graph replay of the same
+// call starts from zero. Returns the chunk index, or K when none is left.
+// Claims need no ordering: they only pick work; results are published by
+// arrive_piece.
+__device__ __forceinline__ int64_t claim_chunk(unsigned long long* ctr, unsigned long long tag48,
+                                               int64_t K, int64_t launched) {
+  const unsigned long long tag = claim_tag(tag48);
+  unsigned long long old = atomicAdd(ctr, 1ull);
+  if ((old >> 20) != tag) {  // the stale word absorbs the add; the install replaces it
+    if (!install_tag(ctr, tag, 20, launched + 64)) return K;
+    old = atomicAdd(ctr, 1ull);
+  }
+  const int64_t cnt = (int64_t)(old & 0xfffffull);
+  if (cnt == K + launched - 1) store_relaxed(ctr, tag << 20);
+  return cnt < K ? cnt : K;
+}
+
+// Unit stream of one call, written by stream position i: P[i] (first unit,
+// P[B] = U), Ls[i] (clamped length) and ord[i] (sequence index). Sequences
+// whose per-head unit count exceeds two tail chunks come first, the others
+// after them, each group in index order; with no tail the order is the index
+// order. Three block passes over the lengths: the unit total (which fixes the
+// plan and the threshold), the long sequences' count and units, and a prefix
+// scan placing every sequence. All NT threads call it; misc holds
+// 3 + 3 * NT / 32 ints.
+__device__ __forceinline__ void warp_scan3(int& a, int& b, int& c, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ta = __shfl_up_sync(0xffffffffu, a, o);
+    const int tb = __shfl_up_sync(0xffffffffu, b, o);
+    const int tc = __shfl_up_sync(0xffffffffu, c, o);
+    if (lane >= o) {
+      a += ta;
+      b += tb;
+      c += tc;
+    }
+  }
+}
+
+template <int NT>
+__device__ int64_t plan_dyn_stream(const AttnParams& p, int* P, int* Ls, int* ord, int* misc,
+                                   int64_t launched, int tile_units, DynPlan& pl) {
+  constexpr int NWARP = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int B = p.B, KVH = p.KVH;
+  auto units_of = [&](int len) { return (len + kUnitTokens - 1) / kUnitTokens; };
+  // pass 1: unit total (lengths kept by index in Ls for pass 2)
+  int part = 0;
+  for (int b = tid; b < B; b += NT) {
+    const int len = checked_length(p.lengths, b, p.max_length);
+    Ls[b] = len;
+    part += units_of(len) * KVH;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (lane == 0) misc[3 + warp] = part;
+  __syncthreads();
+  int U = 0;
+#pragma unroll
+  for (int w = 0; w < NWARP; ++w) U += misc[3 + w];
+  __syncthreads();
+  pl = make_dyn_plan(U, launched, tile_units);
+  const int64_t thr64 = pl.K > 0 ? 2 * (pl.Ut / pl.K) : 0x7fffffff;
+  const int thr = (int)(thr64 < 0x7fffffff ? thr64 : 0x7fffffff);
+  // pass 2: long sequences' count and units
+  int fc = 0, fu = 0;
+  for (int b = tid; b < B; b += NT) {
+    const int nu = units_of(Ls[b]);
+    if (nu > thr) {
+      ++fc;
+      fu += nu * KVH;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    fc += __shfl_xor_sync(0xffffffffu, fc, o);
+    fu += __shfl_xor_sync(0xffffffffu, fu, o);
+  }
+  if (lane == 0) {
+    misc[3 + warp] = fc;
+    misc[3 + NWARP + warp] = fu;
+  }
+  __syncthreads();
+  int FL = 0, NL = 0;
+#pragma unroll
+  for (int w = 0; w < NWARP; ++w) {
+    FL += misc[3 + w];
+    NL += misc[3 + NWARP + w];
+  }
+  __syncthreads();
+  // pass 3: place every sequence (lengths re-read: Ls is rewritten by position)
+  int off_f = 0, off_fu = 0, off_a = 0;
+  for (int base = 0; base < B; base += NT) {
+    const int b = base + tid;
+    int len = 0, nu = 0, f = 0;
+    if (b < B) {
+      len = checked_length(p.lengths, b, p.max_length);
+      nu = units_of(len) * KVH;
+      f = units_of(len) > thr ? 1 : 0;
+    }
+    int sf = f, sfu = f ? nu : 0, sa = nu;
+    warp_scan3(sf, sfu, sa, lane);
+    if (lane == 31) {
+      misc[3 + warp] = sf;
+      misc[3 + NWARP + warp] = sfu;
+      misc[3 + 2 * NWARP + warp] = sa;
+    }
+    __syncthreads();
+    int ef = off_f + sf - f, efu = off_fu + sfu - (f ? nu : 0), ea = off_a + sa - nu;
+    int tf = 0, tfu = 0, ta = 0;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) {
+      const int a0 = misc[3 + w], a1 = misc[3 + NWARP + w], a2 = misc[3 + 2 * NWARP + w];
+      if (w < warp) {
+        ef += a0;
+        efu += a1;
+        ea += a2;
+      }
+      tf += a0;
+      tfu += a1;
+      ta += a2;
+    }
+    if (b < B) {
+      const int pos = f ? ef : FL + (b - ef);
+      P[pos] = f ? efu : NL + (ea - efu);
+      Ls[pos] = len;
+      ord[pos] = b;
+    }
+    off_f += tf;
+    off_fu += tfu;
+    off_a += ta;
+    __syncthreads();
+  }
+  if (tid == 0) P[B] = U;
+  __syncthreads();
+  return U;
+}
+
+// What the producer tells the math warps about the tile in a stage.
+struct TileRecord {
+  int b, h;          // segment (sequence, kv head)
+  int ntok;          // valid tokens in the tile
+  int flags;         // kRecFirst | kRecLast | kRecWhole | kRecEnd
+  int slot;          // partial slot of the piece (non-whole pieces)
+  int pieces;        // pieces of the segment (arrival count)
+  long long w_first; // first worker of the segment
+  long long w_last;  // last worker of the segment
+  int first_slot;    // slot of the segment's piece in w_first
+  int pad;
+};
+// kRecOpen: the piece that starts here will not be a whole segment.
+constexpr int kRecFirst = 1, kRecLast = 2, kRecWhole = 4, kRecEnd = 8, kRecOpen = 16;
+
+// Work queued by the math warps for the epilogue warp: the tag install of a
+// piece's counter when the piece starts, its arrival when it ends, the end.
+struct PieceHandoff {
+  long long w_first, w_last;  // workers of the segment
+  int b, h;                   // segment
+  int pieces;                 // arrival count of the segment
+  int first_slot;             // slot of the segment's piece in w_first
+  int kind;                   // kHandArrive | kHandInstall | kHandEnd
+  int pad;
+};
+constexpr int kHandArrive = 0, kHandInstall = 1, kHandEnd = 2;
+constexpr int kHandoffDepth = 8;
+constexpr int kDynMisc = 32;  // ints of per-CTA scratch
+
+template <class M>
+struct DynStreamK {
+  static_assert(M::LAYOUT == kTma128B, "dynamic kernel stages with TMA");
+  static constexpr int D = M::D, GP = M::GP, NW = M::NW, STAGES = M::STAGES;
+  static constexpr int NT = (NW + 2) * 32;  // math warps, producer, epilogue
+  static constexpr int HALVES = D / 64;
+  static constexpr int UNIT_BYTES = 2 * kUnitTokens * D * 2;
+  static constexpr int MERGE_FLOATS = NW * GP * (D + 2);
+  static size_t smem_bytes(int B) {
+    return 1024 + (size_t)STAGES * M::STAGE_BYTES + (size_t)MERGE_FLOATS * 4 +
+           (size_t)(3 * B + 1 + kDynMisc) * 4 + (2 * STAGES + 2 * kHandoffDepth) * 8 + 16 +
+           (size_t)STAGES * sizeof(TileRecord) + kHandoffDepth * sizeof(PieceHandoff) + 16;
+  }
+  // partial slots: two per worker (static workers + tail chunks)
+  static int64_t slots(int64_t launched) { return 2 * launched * (1 + kTailChunksPerCta); }
+};
+
+template <class M>
+__global__ void __launch_bounds__(DynStreamK<M>::NT, 2)
+attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
+                    const __grid_constant__ CUtensorMap vmap) {
+  using T = typename M::T;
+  using K = DynStreamK<M>;
+  constexpr int D = M::D, GP = M::GP, NW = M::NW, STAGES = M::STAGES, NT = K::NT;
+  constexpr int TILE = M::TILE, TU = M::TILE_UNITS;
+  constexpr int SLOT_FLOATS = GP * (D + 2);
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* ms = reinterpret_cast<float*>(smem + (size_t)STAGES * M::STAGE_BYTES);
+  float* ls = ms + NW * GP;
+  float* accs = ls + NW * GP;
+  int* P = reinterpret_cast<int*>(accs + NW * GP * D);  // by stream position
+  int* Ls = P + p.B + 1;
+  int* ord = Ls + p.B;
+  int* misc = ord + p.B;  // [kDynMisc]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(misc + kDynMisc) + 7) & ~uintptr_t(7));
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* hf_full = bars + 2 * STAGES;  // hand-off queue to the epilogue warp
+  uint64_t* hf_empty = hf_full + kHandoffDepth;
+  TileRecord* recs = reinterpret_cast<TileRecord*>(
+      (reinterpret_cast<uintptr_t>(hf_empty + kHandoffDepth) + 15) & ~uintptr_t(15));
+  PieceHandoff* hand = reinterpret_cast<PieceHandoff*>(recs + STAGES);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int KVH = p.KVH;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
+    for (int j = 0; j < kHandoffDepth; ++j) {
+      mbar_init(&hf_full[j], NW);
+      mbar_init(&hf_empty[j], 1);
+    }
+    fence_barrier_init();
+  }
+  launch_dependents();
+  grid_dependency_wait();  // every global access comes after this
+  static_assert(3 + 3 * (NT / 32) <= kDynMisc, "plan scratch");
+  DynPlan pl;
+  const int64_t U = plan_dyn_stream<NT>(p, P, Ls, ord, misc, gridDim.x, TU, pl);
+  for (int i = blockIdx.x; i < p.B; i += gridDim.x) {
+    if (Ls[i] == 0) {
+      T* o = static_cast<T*>(p.out) + (int64_t)ord[i] * p.H * D;
+      for (int j = tid; j < p.H * D; j += NT) o[j] = Elem<T>::from_f(0.f);
+    }
+  }
+  if (U == 0) return;
+  const bool has_static = (int64_t)blockIdx.x < pl.gs;
+  if (!has_static && pl.K == 0) return;
+  unsigned long long* claim_ctr = p.counters + (int64_t)p.B * KVH;  // one word after arrivals
+  auto stage_k = [&](int s) { return smem + (size_t)s * M::STAGE_BYTES; };
+
+  if (warp == NW) {
+    // ---------------- producer warp: schedule + TMA ----------------
+    int k = 0;  // tiles issued
+    auto next_stage = [&](int& s) {
+      s = k % STAGES;
+      const uint32_t use = (uint32_t)(k / STAGES);
+      if (use > 0) mbar_wait(&empty[s], (use - 1) & 1);
+    };
+    // Tail chunks are claimed when the last tile of the current worker has
+    // been issued, i.e. STAGES tiles before the math warps run out of work.
+    auto claim = [&]() -> int64_t {
+      int64_t c = pl.K;
+      if (pl.K > 0 && lane == 0) c = claim_chunk(claim_ctr, p.call_tag, pl.K, gridDim.x);
+      return __shfl_sync(0xffffffffu, c, 0);
+    };
+    int64_t w = has_static ? (int64_t)blockIdx.x : -1;
+    if (w < 0) {
+      const int64_t c0 = claim();
+      w = c0 < pl.K ? pl.gs + c0 : -1;
+    }
+    while (w >= 0) {
+      const int64_t wb = pl.begin(w), we = pl.begin(w + 1);
+      Cursor c;
+      cursor_locate(c, P, p.B, KVH, wb);
+      bool piece_first = true;
+      int64_t next_w = -1;
+      while (true) {
+        int s;
+        next_stage(s);
+        const int64_t te = cursor_tile_end<TU>(c, we);
+        const int nunits = (int)(te - c.u);
+        const int tok0 = (int)(c.u - c.seg) * kUnitTokens;
+        const bool seg_end = te == c.seg + c.nu;
+        const bool last = seg_end || te == we;
+        if (lane == 0) {
+          TileRecord r{};
+          r.b = ord[c.b];
+          r.h = c.h;
+          const int rem = Ls[c.b] - tok0;
+          r.ntok = nunits * kUnitTokens < rem ? nunits * kUnitTokens : rem;
+          r.flags = (piece_first ? kRecFirst : 0) | (last ? kRecLast : 0);
+          if (piece_first && !(c.u == c.seg && c.seg + c.nu <= we)) r.flags |= kRecOpen;
+          if (last) {
+            // The piece started at the worker's begin or at the segment's.
+            const int64_t pstart = wb > c.seg ? wb : c.seg;
+            if (seg_end && pstart == c.seg) {
+              r.flags |= kRecWhole;
+            } else {
+              const int64_t S0 = c.seg, S1 = c.seg + c.nu;
+              const int64_t w0 = pl.owner(S0), w1 = pl.owner(S1 - 1);
+              r.slot = (int)(2 * w + (pstart == wb ? 0 : 1));
+              r.pieces = (int)(w1 - w0 + 1);
+              r.w_first = w0;
+              r.w_last = w1;
+              r.first_slot = (int)(2 * w0 + (pl.begin(w0) < S0 ? 1 : 0));
+            }
+          }
+          recs[s] = r;
+        }
+        // page lookups: lane i < nunits stages unit i of the tile
+        bool ok = false;
+        int row0 = 0;
+        if (lane < nunits) {
+          const int t = tok0 + lane * kUnitTokens;
+          const int pi = p.bs_shift >= 0 ? (t >> p.bs_shift) : t / p.block_size;
+          const int off = t - pi * p.block_size;
+          const int page = __ldg(p.tables + (int64_t)ord[c.b] * p.table_width + pi);
+          if (page < 0 || (int64_t)page >= p.num_blocks) {
+            raise_error(0x1u);
+          } else {
+            ok = true;
+            row0 = page * p.block_size + off;
+          }
+        }
+        const unsigned okmask = __ballot_sync(0xffffffffu, ok);
+        if (lane == 0) {
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(&full[s], (uint32_t)__popc(okmask) * K::UNIT_BYTES);
+        }
+        __syncwarp();
+        if (ok) {
+          unsigned char* sk = stage_k(s);
+          unsigned char* sv = sk + M::TILE_BYTES;
+#pragma unroll
+          for (int hf = 0; hf < K::HALVES; ++hf) {
+            const int dst = hf * (TILE * 128) + lane * kUnitTokens * 128;
+            tma_load_3d(sk + dst, &kmap, hf * 64, c.h, row0, &full[s]);
+            tma_load_3d(sv + dst, &vmap, hf * 64, c.h, row0, &full[s]);
+          }
+        }
+        ++k;
+        piece_first = last;  // a piece end makes the next tile a piece start
+        if (te >= we) {
+          const int64_t cn = claim();
+          next_w = cn < pl.K ? pl.gs + cn : -1;
+          break;
+        }
+        cursor_advance(c, te, we, P, KVH);
+      }
+      w = next_w;
+    }
+    // end record
+    int s;
+    next_stage(s);
+    if (lane == 0) {
+      TileRecord r{};
+      r.flags = kRecEnd;
+      recs[s] = r;
+      mbar_arrive_expect_tx(&full[s], 0);
+    }
+    return;
+  }
+
+  if (warp == NW + 1) {
+    // ---------------- epilogue warp: tag installs, arrivals, merges ----------
+    if (lane == 0 && pl.K > 0) install_tag(claim_ctr, claim_tag(p.call_tag), 20, gridDim.x + 64);
+    for (int hk = 0;; ++hk) {
+      const int j = hk % kHandoffDepth;
+      mbar_wait(&hf_full[j], (uint32_t)(hk / kHandoffDepth) & 1);
+      const PieceHandoff r = hand[j];
+      if (r.kind == kHandEnd) break;
+      unsigned long long* ctr = p.counters + ((int64_t)r.b * KVH + r.h);
+      if (r.kind == kHandInstall) {
+        if (lane == 0) install_tag(ctr, p.call_tag, 16, (int64_t)gridDim.x * 8 + 64);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&hf_empty[j]);
+        continue;
+      }
+      int last = 0;
+      if (lane == 0) last = arrive_installed(ctr, p.call_tag, (unsigned)r.pieces);
+      last = __shfl_sync(0xffffffffu, last, 0);
+      __syncwarp();  // lane 0's acquire orders the other lanes' slot reads
+      if (last) {
+        T* outp = static_cast<T*>(p.out) + ((int64_t)r.b * p.H + (int64_t)r.h * p.G) * D;
+        merge_slots<T, GP, D, 32, 48>(p.partials, outp, p.G, r.w_first, r.w_last, r.first_slot,
+                                      lane);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&hf_empty[j]);
+    }
+    return;
+  }
+
+  // ---------------- math warps ----------------
+  typename M::State st;
+  auto sync_math = [] { named_bar_sync(1, NW * 32); };
+  int hk = 0;  // pieces handed to the epilogue warp
+  // Queue entry hk % depth: warp 0 waits until the epilogue warp has taken
+  // the entry's previous use and writes it; each math warp's lane 0 arrives
+  // after its warp's slot stores (release at CTA scope; the epilogue warp's
+  // gpu-scope release in arrive_piece then covers them).
+  auto hand_off = [&](const PieceHandoff& h) {
+    const int j = hk % kHandoffDepth;
+    if (warp == 0) {
+      const uint32_t use = (uint32_t)(hk / kHandoffDepth);
+      if (use > 0) mbar_wait(&hf_empty[j], (use - 1) & 1);
+      if (lane == 0) hand[j] = h;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&hf_full[j]);
+    ++hk;
+  };
+  for (int k = 0;; ++k) {
+    const int s = k % STAGES;
+    mbar_wait(&full[s], (uint32_t)(k / STAGES) & 1);
+    const TileRecord r = recs[s];
+    if (r.flags & kRecEnd) break;
+    unsigned char* sk = stage_k(s);
+    unsigned char* sv = sk + M::TILE_BYTES;
+    const int r0 = warp * M::WT;
+    if (r0 < r.ntok && r0 + M::WT > r.ntok) {
+      for (int i = lane; i < (r0 + M::WT - r.ntok) * (D / 8); i += 32) {
+        const int row = r.ntok + i / (D / 8), col = i % (D / 8);
+        *reinterpret_cast<uint4*>(sv + M::offset(row, col)) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+    }
+    if ((r.flags & (kRecFirst | kRecOpen)) == (kRecFirst | kRecOpen))
+      hand_off(PieceHandoff{0, 0, r.b, r.h, 0, 0, kHandInstall, 0});
+    if (r.flags & kRecFirst) M::begin_piece(st, p, r.b, r.h);
+    M::compute_tile(st, p, sk, sv, r.ntok, nullptr);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    if (r.flags & kRecLast) {
+      M::store_state(st, ms, ls, accs);
+      sync_math();
+      T* outp = static_cast<T*>(p.out) + ((int64_t)r.b * p.H + (int64_t)r.h * p.G) * D;
+      const bool whole = r.flags & kRecWhole;
+      float* slot = p.partials + (size_t)r.slot * SLOT_FLOATS;
+      for (int idx = tid; idx < GP * D; idx += NW * 32) {
+        const int g = idx / D, d = idx - g * D;
+        float M_ = -INFINITY;
+#pragma unroll
+        for (int ww = 0; ww < NW; ++ww) M_ = fmaxf(M_, ms[ww * GP + g]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < NW; ++ww) {
+          const float mw = ms[ww * GP + g];
+          const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M_);
+          L = fmaf(ls[ww * GP + g], f, L);
+          O = fmaf(accs[(ww * GP + g) * D + d], f, O);
+        }
+        if (whole) {
+          if (g < p.G) outp[g * D + d] = Elem<T>::from_f(O / L);
+        } else {
+          slot[2 * GP + g * D + d] = O;
+          if (d == 0) {
+            slot[g] = M_;
+            slot[GP + g] = L;
+          }
+        }
+      }
+      if (!whole)
+        hand_off(PieceHandoff{r.w_first, r.w_last, r.b, r.h, r.pieces, r.first_slot, kHandArrive,
+                              0});
+      sync_math();  // ms/ls/accs are free for the next piece
+    }
+  }
+  hand_off(PieceHandoff{0, 0, 0, 0, 0, 0, kHandEnd, 0});
+}
+
+}  // namespace pdb

@@ -19,6 +19,7 @@
 #include "paged_decode_b200.h"
 #include "attention.cuh"
 #include "attention_tma.cuh"
+#include "attention_dyn.cuh"
 #include "rope_kv_write.cuh"
 
 namespace {
@@ -102,9 +103,10 @@ struct FastKernel {
   void (*launch)(const pdb::AttnParams&, int grid, size_t smem, cudaStream_t,
                  const CUtensorMap* kmap, const CUtensorMap* vmap);
   size_t (*smem)(int B);
-  int gp;       // heads per kv head kept in partial slots
-  int threads;  // CTA size
-  bool tma;     // needs K/V tensor maps
+  int gp;             // heads per kv head kept in partial slots
+  int threads;        // CTA size
+  bool tma;           // needs K/V tensor maps
+  int slots_per_cta;  // partial slots per launched CTA
 };
 
 template <class M>
@@ -116,7 +118,7 @@ void launch_streamk(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_
 template <class M>
 FastKernel make_fast() {
   return FastKernel{reinterpret_cast<const void*>(&pdb::attn_streamk_kernel<M>),
-                    &launch_streamk<M>, &pdb::StreamK<M>::smem_bytes, M::GP, M::NT, false};
+                    &launch_streamk<M>, &pdb::StreamK<M>::smem_bytes, M::GP, M::NT, false, 2};
 }
 
 // Launch with programmatic stream serialization: the kernel may begin while
@@ -148,7 +150,21 @@ void launch_tma(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st
 template <class M>
 FastKernel make_tma() {
   return FastKernel{reinterpret_cast<const void*>(&pdb::attn_tma_kernel<M>), &launch_tma<M>,
-                    &pdb::TmaStreamK<M>::smem_bytes, M::GP, pdb::TmaStreamK<M>::NT, true};
+                    &pdb::TmaStreamK<M>::smem_bytes, M::GP, pdb::TmaStreamK<M>::NT, true, 2};
+}
+
+template <class M>
+void launch_dyn(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st,
+                const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  launch_pdl(pdb::attn_tma_dyn_kernel<M>, dim3(grid), dim3(pdb::DynStreamK<M>::NT), smem, st, p,
+             *kmap, *vmap);
+}
+
+template <class M>
+FastKernel make_dyn() {
+  return FastKernel{reinterpret_cast<const void*>(&pdb::attn_tma_dyn_kernel<M>), &launch_dyn<M>,
+                    &pdb::DynStreamK<M>::smem_bytes, M::GP, pdb::DynStreamK<M>::NT, true,
+                    2 * (1 + pdb::kTailChunksPerCta)};
 }
 
 // cuTensorMapEncodeTiled from the driver (resolved once through the runtime,
@@ -218,8 +234,25 @@ bool pick_simt(int D, int G, FastKernel* out) {
   }
 }
 
-// Tensor-core inner loop with a TMA producer warp (FP16, block_size % 16 == 0).
-// Stage depths keep two CTAs resident per SM.
+// Tensor-core inner loop, TMA producer warp and dynamic tail (FP16,
+// block_size % 16 == 0). Stage depths keep two CTAs resident per SM.
+bool pick_dyn(int D, int G, FastKernel* out) {
+  if (G > 8) return false;
+  const bool g4 = G <= 4;
+  if (D == 128) {
+    *out = g4 ? make_dyn<pdb::MmaMath<128, 4, 3, pdb::kTma128B>>()
+              : make_dyn<pdb::MmaMath<128, 8, 2, pdb::kTma128B>>();
+    return true;
+  }
+  if (D == 64) {
+    *out = g4 ? make_dyn<pdb::MmaMath<64, 4, 6, pdb::kTma128B>>()
+              : make_dyn<pdb::MmaMath<64, 8, 5, pdb::kTma128B>>();
+    return true;
+  }
+  return false;
+}
+
+// Same with the static schedule only (two partial slots per CTA).
 bool pick_tma(int D, int G, FastKernel* out) {
   if (G > 8) return false;
   const bool g4 = G <= 4;
@@ -258,7 +291,7 @@ bool streamk_shape_ok(int64_t B, int64_t KVH) {
 }
 
 // Kernel families a caller can pin (pdb_impl_t) below AUTO/FAST.
-enum Family { kAny = 0, kSimtOnly = 1, kCpAsyncMma = 2 };
+enum Family { kAny = 0, kSimtOnly = 1, kCpAsyncMma = 2, kStaticTma = 3 };
 
 // The stream-K kernel for this shape: FP16 tensor cores fed by TMA when the
 // pool allows (block_size % 16 == 0, rows addressable by 32-bit coordinates,
@@ -269,15 +302,16 @@ bool fast_applicable(int64_t B, int64_t H, int64_t KVH, int64_t D, int dtype, Fa
                      int family = kAny, int64_t bs = 16, int64_t N = 1) {
   if (!streamk_shape_ok(B, KVH)) return false;
   const int G = (int)(H / KVH);
+  const bool tma_ok = bs % pdb::kUnitTokens == 0 && N * bs < (int64_t(1) << 31) &&
+                      tensor_map_encoder() != nullptr;
   if (dtype == PDB_DTYPE_FLOAT16) {
-    if (family == kAny && bs % pdb::kUnitTokens == 0 && N * bs < (int64_t(1) << 31) &&
-        tensor_map_encoder() && pick_tma((int)D, G, k))
-      return true;
+    if (family == kAny && tma_ok && pick_dyn((int)D, G, k)) return true;
+    if (family == kStaticTma) return tma_ok && pick_tma((int)D, G, k);
     if (family != kSimtOnly && pick_mma((int)D, G, k)) return true;
     if (family == kCpAsyncMma) return false;
     return pick_simt<__half>((int)D, G, k);
   }
-  if (family == kCpAsyncMma) return false;
+  if (family == kCpAsyncMma || family == kStaticTma) return false;
   return pick_simt<float>((int)D, G, k);
 }
 
@@ -299,11 +333,13 @@ int64_t fast_grid(int dev, const FastKernel& k, int64_t B, int64_t KVH, int64_t 
 struct FastWs {
   size_t counters_off, partials_off, total;
 };
-FastWs fast_ws_layout(int64_t B, int64_t KVH, int64_t D, int gp, int64_t grid) {
+// [arrival counters: B*KVH words + 1 tail-claim word][partial slots]
+FastWs fast_ws_layout(int64_t B, int64_t KVH, int64_t D, const FastKernel& k, int64_t grid) {
   FastWs w;
   w.counters_off = 0;
-  w.partials_off = align256((size_t)(B * KVH) * sizeof(unsigned long long));
-  w.total = w.partials_off + align256((size_t)(2 * grid) * gp * (D + 2) * sizeof(float));
+  w.partials_off = align256((size_t)(B * KVH + 1) * sizeof(unsigned long long));
+  w.total = w.partials_off +
+            align256((size_t)(k.slots_per_cta * grid) * k.gp * (D + 2) * sizeof(float));
   return w;
 }
 
@@ -390,9 +426,10 @@ size_t pdb_paged_attention_workspace_size(int64_t batch, int64_t heads, int64_t 
   // The pool's block size is not known here, so cover every stream-K kernel
   // that a call of this shape may select.
   const int G = (int)(heads / kv_heads);
-  FastKernel cand[3];
+  FastKernel cand[4];
   int n = 0;
   if (dtype == PDB_DTYPE_FLOAT16) {
+    if (tensor_map_encoder() && pick_dyn((int)head_dim, G, &cand[n])) ++n;
     if (tensor_map_encoder() && pick_tma((int)head_dim, G, &cand[n])) ++n;
     if (pick_mma((int)head_dim, G, &cand[n])) ++n;
     if (pick_simt<__half>((int)head_dim, G, &cand[n])) ++n;
@@ -402,7 +439,7 @@ size_t pdb_paged_attention_workspace_size(int64_t batch, int64_t heads, int64_t 
   for (int i = 0; i < n; ++i) {
     const int64_t grid = fast_grid(dev, cand[i], batch, kv_heads, max_length);
     if (grid > 0) {
-      const size_t f = fast_ws_layout(batch, kv_heads, head_dim, cand[i].gp, grid).total;
+      const size_t f = fast_ws_layout(batch, kv_heads, head_dim, cand[i], grid).total;
       if (f > need) need = f;
     }
   }
@@ -429,7 +466,7 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
   if (rc) return rc;
   if (!q || !k_pool || !v_pool || !tables || !lengths || !out)
     return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  if (impl < PDB_IMPL_AUTO || impl > PDB_IMPL_MMA)
+  if (impl < PDB_IMPL_AUTO || impl > PDB_IMPL_TMA_STATIC)
     return fail(PDB_ERR_INVALID_ARGUMENT, "unknown kernel selection");
   int dev = 0;
   if ((rc = current_device(&dev))) return rc;
@@ -449,7 +486,10 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
     return fail(PDB_ERR_WORKSPACE, "workspace must be 256-byte aligned");
 
   FastKernel fk;
-  const int family = impl == PDB_IMPL_SIMT ? kSimtOnly : impl == PDB_IMPL_MMA ? kCpAsyncMma : kAny;
+  const int family = impl == PDB_IMPL_SIMT         ? kSimtOnly
+                     : impl == PDB_IMPL_MMA        ? kCpAsyncMma
+                     : impl == PDB_IMPL_TMA_STATIC ? kStaticTma
+                                                   : kAny;
   const bool fast_ok = fast_applicable(B, H, KVH, D, dtype, &fk, family, bs, N) &&
                        aligned16(q) && aligned16(k_pool) && aligned16(v_pool);
   if (impl != PDB_IMPL_AUTO && impl != PDB_IMPL_GENERIC && !fast_ok)
@@ -458,7 +498,7 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
   if (fast_ok && impl != PDB_IMPL_GENERIC) {
     const int64_t grid = fast_grid(dev, fk, B, KVH, max_length);
     if (grid <= 0) return fail(PDB_ERR_CUDA, "fast kernel cannot be resident on this device");
-    const FastWs ws = fast_ws_layout(B, KVH, D, fk.gp, grid);
+    const FastWs ws = fast_ws_layout(B, KVH, D, fk, grid);
     if (!workspace || workspace_bytes < ws.total)
       return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) +
                                          " bytes");
@@ -506,14 +546,16 @@ int pdb_paged_attention_noalloc(const void* q, const void* k_pool, const void* v
   int dev = 0;
   if ((rc = current_device(&dev))) return rc;
   FastKernel fk;
-  if (!(fast_applicable(B, H, KVH, D, dtype, &fk, kAny, bs, N) && aligned16(q) &&
-        aligned16(k_pool) && aligned16(v_pool)))
+  const bool fits = fast_applicable(B, H, KVH, D, dtype, &fk, kStaticTma, bs, N) ||
+                    fast_applicable(B, H, KVH, D, dtype, &fk, kCpAsyncMma, bs, N) ||
+                    fast_applicable(B, H, KVH, D, dtype, &fk, kSimtOnly, bs, N);
+  if (!(fits && aligned16(q) && aligned16(k_pool) && aligned16(v_pool)))
     return fail(PDB_ERR_INVALID_ARGUMENT,
                 "pdb_paged_attention_noalloc: shape or alignment needs the generic kernel; "
                 "use pdb_paged_attention with a workspace");
   const int64_t grid = fast_grid(dev, fk, B, KVH, max_length);
   if (grid <= 0) return fail(PDB_ERR_CUDA, "fast kernel cannot be resident on this device");
-  const FastWs ws = fast_ws_layout(B, KVH, D, fk.gp, grid);
+  const FastWs ws = fast_ws_layout(B, KVH, D, fk, grid);
   if (ws.total > kNoAllocScratchBytes)
     return fail(PDB_ERR_WORKSPACE,
                 "pdb_paged_attention_noalloc: this shape needs " + std::to_string(ws.total) +
@@ -647,6 +689,20 @@ int pdb_read_device_errors(uint32_t* flags, int clear) {
   }
   *flags = v;
   return PDB_OK;
+}
+
+int64_t pdb_debug_dyn_partition(int64_t units, int64_t launched, int64_t* ranges,
+                                int64_t max_workers) {
+  if (units <= 0 || launched <= 0 || !ranges) return -1;
+  const pdb::DynPlan pl = pdb::make_dyn_plan(units, launched, 4);
+  const int64_t nw = pl.gs + pl.K;
+  if (nw > max_workers) return -1;
+  for (int64_t w = 0; w < nw; ++w) {
+    ranges[3 * w] = pl.begin(w);
+    ranges[3 * w + 1] = pl.begin(w + 1);
+    ranges[3 * w + 2] = w < pl.gs ? 0 : 1;
+  }
+  return pl.gs;
 }
 
 int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch, int64_t kv_heads,

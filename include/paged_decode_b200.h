@@ -56,11 +56,12 @@ typedef enum {
 typedef enum {
   PDB_IMPL_AUTO = 0,    /* stream-K kernel when the shape allows, else generic  */
   PDB_IMPL_FAST = 1,    /* stream-K, GQA-shared tiles: FP16 head_dim 64/128 on
-                           tensor cores (TMA-fed when block_size % 16 == 0),
-                           SIMT otherwise                                      */
+                           tensor cores (TMA-fed with a dynamically claimed
+                           tail when block_size % 16 == 0), SIMT otherwise     */
   PDB_IMPL_GENERIC = 2, /* any head_dim <= 256 / any alignment, split + combine */
   PDB_IMPL_SIMT = 3,    /* stream-K with the SIMT inner loop only               */
-  PDB_IMPL_MMA = 4      /* stream-K, tensor cores fed by cp.async (no TMA)      */
+  PDB_IMPL_MMA = 4,     /* stream-K, tensor cores fed by cp.async (no TMA)      */
+  PDB_IMPL_TMA_STATIC = 5 /* TMA-fed tensor cores, static schedule only       */
 } pdb_impl_t;
 
 /* Bits of the per-device error word (pdb_read_device_errors). */
@@ -205,6 +206,17 @@ PDB_API int pdb_read_device_errors(uint32_t* flags, int clear);
  */
 PDB_API int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch,
                             int64_t kv_heads, int64_t grid, int64_t* ranges);
+
+/*
+ * Host-side copy of the default FP16 kernel's worker partition, for tests.
+ * No reference counterpart. For `units` 16-token units and `launched` CTAs,
+ * writes per worker w: ranges[3w], ranges[3w+1] = its [begin, end) and
+ * ranges[3w+2] = 0 (static range of CTA w) or 1 (dynamically claimed tail
+ * chunk). Returns the number of static workers, or -1 (bad arguments or more
+ * than max_workers workers).
+ */
+PDB_API int64_t pdb_debug_dyn_partition(int64_t units, int64_t launched, int64_t* ranges,
+                                        int64_t max_workers);
 
 /* CTAs the fast kernel launches per call on the current device for this
  * shape (0 when the fast kernel does not apply). No reference counterpart. */

@@ -146,3 +146,25 @@ def test_install_rebinds_module_global(pkg):
     mod.cuda_paged_attention = None
     pkg.install(mod)
     assert mod.cuda_paged_attention is pkg.cuda_paged_attention
+
+
+@pytest.mark.parametrize("units,launched", [(1, 296), (15, 296), (16, 296), (2048, 296),
+                                            (9471, 296), (9472, 296), (40000, 296),
+                                            (163000, 296), (20000, 148), (7, 1), (100000, 1)])
+def test_dynamic_partition_covers_units(lib, units, launched):
+    """Static ranges + tail chunks partition [0, units) into non-empty,
+    ordered ranges (no division by an empty tail), tail chunks >= one tile."""
+    ranges = np.zeros(3 * launched * 6, dtype=np.int64)
+    gs = lib.pdb_debug_dyn_partition(units, launched, ranges.ctypes.data, launched * 6)
+    assert gs >= 1
+    r = ranges.reshape(-1, 3)
+    nw = int(np.count_nonzero(r[:, 1]))
+    r = r[:nw]
+    assert r[0, 0] == 0 and r[-1, 1] == units
+    assert np.all(r[1:, 0] == r[:-1, 1])
+    assert np.all(r[:, 1] > r[:, 0])
+    assert np.all(r[:gs, 2] == 0) and np.all(r[gs:, 2] == 1)
+    tail = r[gs:]
+    if len(tail):
+        assert np.all(tail[:, 1] - tail[:, 0] >= 16)  # four 64-token tiles
+        assert tail[0, 0] == units - units // 16

@@ -17,8 +17,9 @@ pytestmark = pytest.mark.gpu
 mg = golden_module()
 W = import_module("workloads")
 _lib = import_module("_lib")
-IMPLS = [_lib.IMPL_AUTO, _lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT, _lib.IMPL_MMA]
-STREAMK = (_lib.IMPL_FAST, _lib.IMPL_SIMT, _lib.IMPL_MMA)
+IMPLS = [_lib.IMPL_AUTO, _lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT, _lib.IMPL_MMA,
+         _lib.IMPL_TMA_STATIC]
+STREAMK = (_lib.IMPL_FAST, _lib.IMPL_SIMT, _lib.IMPL_MMA, _lib.IMPL_TMA_STATIC)
 
 
 def gold(name):
@@ -62,7 +63,7 @@ def test_edge_cases(pkg, cuda, impl):
         assert_parity(out, case["out"], case["spec"]["name"])
         assert torch.all(out[lengths == 0] == 0)
         ran += 1
-    assert ran >= (4 if impl == _lib.IMPL_MMA else 8)
+    assert ran >= (4 if impl in (_lib.IMPL_MMA, _lib.IMPL_TMA_STATIC) else 8)
 
 
 @pytest.mark.parametrize("impl", IMPLS)
@@ -85,15 +86,98 @@ def test_stale_pool_bytes_are_never_read(pkg, cuda, dtype, impl):
     assert torch.equal(clean, poisoned)
 
 
-@pytest.mark.parametrize("impl", [_lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT, _lib.IMPL_MMA])
+@pytest.mark.parametrize("impl", [_lib.IMPL_FAST, _lib.IMPL_GENERIC, _lib.IMPL_SIMT, _lib.IMPL_MMA,
+                                  _lib.IMPL_TMA_STATIC])
 def test_repeated_calls_are_deterministic(pkg, cuda, impl):
-    w = W.llama3_8b(batch=24, layers=1)
+    """Bit-identical results call after call (the dynamic tail changes which
+    CTA runs a chunk, not the result)."""
+    w = W.llama3_8b(batch=96, layers=1)
     t = W.materialize(w, cuda)
     outs = [pkg.paged_attention(t.q[0], t.k_pools[0], t.v_pools[0], t.tables, t.lengths,
                                 w.max_length, impl=impl) for _ in range(5)]
     torch.cuda.synchronize()
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+@pytest.mark.parametrize("impl", [_lib.IMPL_FAST, _lib.IMPL_TMA_STATIC, _lib.IMPL_MMA,
+                                  _lib.IMPL_SIMT])
+def test_cuda_graph_replays_match_eager(pkg, cuda, impl):
+    """Calls captured once in a CUDA graph keep their call tags on every
+    replay, so the arrival and tail-claim counters must be back at zero when
+    a call ends. Two calls per graph share the stream's workspace; each replay
+    with fresh queries matches eager calls bit for bit."""
+    w = W.llama3_8b(batch=96, layers=2)
+    t = W.materialize(w, cuda)
+    q = t.q[0].clone()
+    outs = [torch.empty_like(q) for _ in range(2)]
+    s = torch.cuda.Stream()
+
+    def call(i, out=None):
+        return pkg.paged_attention(q, t.k_pools[i], t.v_pools[i], t.tables, t.lengths,
+                                   w.max_length, out=out, impl=impl)
+
+    with torch.cuda.stream(s):
+        call(0, outs[0]), call(1, outs[1])  # workspace and kernel attributes set up
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            call(0, outs[0])
+            call(1, outs[1])
+        gen = torch.Generator(device=cuda).manual_seed(3)
+        for _ in range(3):
+            q.copy_(torch.randn(q.shape, generator=gen, device=cuda).to(q.dtype))
+            g.replay()
+            eager = [call(0), call(1)]
+            s.synchronize()
+            for i in range(2):
+                assert torch.equal(outs[i], eager[i]), f"replay differs from eager (layer {i})"
+    del g
+    assert pkg.read_device_errors() == 0
+
+
+@pytest.mark.parametrize("layout", ["long_last", "long_first", "zeros_mixed"])
+def test_tail_order_with_skewed_lengths(pkg, cuda, layout):
+    """Batches whose long sequences sit at the end (index order would put
+    them in the dynamically scheduled tail), at the start, or mixed with empty
+    sequences: the tensor-core kernels agree with the generic kernel
+    everywhere and with the CPU oracle on the long and the empty sequences."""
+    g = torch.Generator().manual_seed(11)
+    B, H, KVH, D, bs = 160, 32, 8, 128, 16
+    lengths = torch.randint(64, 400, (B,), generator=g).to(torch.int32)
+    if layout == "long_last":
+        lengths[-6:] = torch.tensor([8192, 7000, 6100, 8000, 5000, 7777], dtype=torch.int32)
+    elif layout == "long_first":
+        lengths[:6] = torch.tensor([8192, 7000, 6100, 8000, 5000, 7777], dtype=torch.int32)
+    else:
+        lengths[::7] = 0
+        lengths[3::11] = 6000
+    need = (lengths.to(torch.int64) + bs - 1) // bs
+    width = int(need.max())
+    N = int(need.sum()) + 5
+    perm = torch.randperm(N, generator=g)
+    tables = torch.zeros(B, width, dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(need.tolist()):
+        tables[b, :n] = perm[off:off + n].to(torch.int32)
+        off += n
+    q = torch.randn(B, H, D, generator=g).half()
+    k = torch.randn(N, bs, KVH, D, generator=g).half()
+    v = torch.randn(N, bs, KVH, D, generator=g).half()
+    args = (q.to(cuda), k.to(cuda), v.to(cuda), tables.to(cuda), lengths.to(cuda),
+            int(lengths.max()))
+    generic = pkg.paged_attention(*args, impl=_lib.IMPL_GENERIC).cpu()
+    fast = pkg.paged_attention(*args, impl=_lib.IMPL_FAST).cpu()
+    static = pkg.paged_attention(*args, impl=_lib.IMPL_TMA_STATIC).cpu()
+    assert_parity(fast, generic, f"{layout}: dynamic vs generic")
+    assert_parity(static, generic, f"{layout}: static vs generic")
+    order = torch.argsort(lengths)
+    pick = torch.cat([order[:4], order[-6:]]).unique()
+    tabs, (kp, vp) = subset_pool(tables[pick], lengths[pick], [k, v], bs)
+    lens = lengths[pick]
+    ref = opa.paged_attention(q[pick], kp, vp, tabs, lens, int(lens.max()))
+    assert_parity(fast[pick], ref, f"{layout}: dynamic vs oracle")
+    assert pkg.read_device_errors() == 0
 
 
 def test_smollm_fp16_layer(pkg, cuda):
@@ -119,7 +203,9 @@ def test_llama3_full_batch(pkg, cuda):
     generic = pkg.paged_attention(*args, impl=_lib.IMPL_GENERIC)
     simt = pkg.paged_attention(*args, impl=_lib.IMPL_SIMT)
     mma = pkg.paged_attention(*args, impl=_lib.IMPL_MMA)
-    assert_parity(fast, generic.cpu(), "tma tensor-core vs generic")
+    static = pkg.paged_attention(*args, impl=_lib.IMPL_TMA_STATIC)
+    assert_parity(fast, generic.cpu(), "tma tensor-core (dynamic tail) vs generic")
+    assert_parity(static, generic.cpu(), "tma tensor-core (static) vs generic")
     assert_parity(simt, generic.cpu(), "simt vs generic")
     assert_parity(mma, generic.cpu(), "cp.async tensor-core vs generic")
     order = torch.argsort(w.lengths)
