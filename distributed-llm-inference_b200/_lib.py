@@ -36,6 +36,10 @@ SIGNATURES = {
                                    _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                    _c_i64, _c_int, _c_ptr, _c_size, _c_ptr]),
     "pdb_rope_kv_write_workspace_size": (_c_size, [_c_i64, _c_i64, _c_int]),
+    "pdb_rope_kv_write_decode": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                          _c_ptr, _c_i64, _c_ptr, _c_int, _c_ptr, _c_i64,
+                                          _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
+                                          _c_ptr]),
     "pdb_read_device_errors": (_c_int, [ctypes.POINTER(ctypes.c_uint32), _c_int]),
     "pdb_debug_partition": (_c_i64, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr]),
     "pdb_debug_dyn_partition": (_c_i64, [_c_i64, _c_i64, _c_ptr, _c_i64]),

@@ -404,6 +404,34 @@ int noalloc_scratch(int dev, unsigned char** out) {
   return PDB_OK;
 }
 
+// Launch the prologue over p.num_rows rows: the 16-byte vectorised kernel
+// when each half head row is a whole number of 16-byte chunks and every
+// row buffer is 16-byte aligned, else the scalar kernel.
+int launch_rope(const pdb::RopeParams& p, int dtype, cudaStream_t st) {
+  const int esize = dtype == PDB_DTYPE_FLOAT16 ? 2 : 4;
+  const bool vec_ok = ((int64_t)p.dim * esize) % 32 == 0 && aligned16(p.q) && aligned16(p.k) &&
+                      aligned16(p.v) && aligned16(p.q_out) && aligned16(p.k_out) &&
+                      aligned16(p.k_pool) && aligned16(p.v_pool);
+  if (vec_ok) {
+    constexpr int kRows = 2;
+    const unsigned grid = (unsigned)((p.num_rows + kRows - 1) / kRows);
+    const size_t smem = (size_t)kRows * p.dim * sizeof(float);
+    if (dtype == PDB_DTYPE_FLOAT16)
+      launch_pdl(pdb::rope_kv_write_vec_kernel<__half, kRows>, dim3(grid), dim3(256), smem, st, p);
+    else
+      launch_pdl(pdb::rope_kv_write_vec_kernel<float, kRows>, dim3(grid), dim3(256), smem, st, p);
+  } else {
+    const size_t smem = (size_t)p.dim * sizeof(float);
+    if (dtype == PDB_DTYPE_FLOAT16)
+      pdb::rope_kv_write_kernel<__half><<<(unsigned)p.num_rows, 128, smem, st>>>(p);
+    else
+      pdb::rope_kv_write_kernel<float><<<(unsigned)p.num_rows, 128, smem, st>>>(p);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rope_kv_write launch");
+  return PDB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -651,28 +679,41 @@ int pdb_rope_kv_write(const void* q, const void* k, const void* v, void* q_out, 
   p.heads = (int)heads; p.kv_heads = (int)kv_heads; p.dim = (int)head_dim;
   p.num_blocks = num_blocks; p.block_size = (int)block_size;
   p.num_rows = rows;
-  const int esize = dtype == PDB_DTYPE_FLOAT16 ? 2 : 4;
-  const bool vec_ok = (head_dim * esize) % 32 == 0 && aligned16(q) && aligned16(k) &&
-                      aligned16(v) && aligned16(q_out) && aligned16(k_out) &&
-                      aligned16(k_pool) && aligned16(v_pool);
-  if (vec_ok) {
-    constexpr int kRows = 2;
-    const unsigned grid = (unsigned)((rows + kRows - 1) / kRows);
-    const size_t smem = (size_t)kRows * head_dim * sizeof(float);
-    if (dtype == PDB_DTYPE_FLOAT16)
-      launch_pdl(pdb::rope_kv_write_vec_kernel<__half, kRows>, dim3(grid), dim3(256), smem, st, p);
-    else
-      launch_pdl(pdb::rope_kv_write_vec_kernel<float, kRows>, dim3(grid), dim3(256), smem, st, p);
-  } else {
-    const size_t smem = (size_t)head_dim * sizeof(float);
-    if (dtype == PDB_DTYPE_FLOAT16)
-      pdb::rope_kv_write_kernel<__half><<<(unsigned)rows, 128, smem, st>>>(p);
-    else
-      pdb::rope_kv_write_kernel<float><<<(unsigned)rows, 128, smem, st>>>(p);
-  }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "rope_kv_write launch");
-  return PDB_OK;
+  return launch_rope(p, dtype, st);
+}
+
+int pdb_rope_kv_write_decode(const void* q, const void* k, const void* v, void* q_out,
+                             void* k_out, void* k_pool, void* v_pool, const int32_t* tables,
+                             int64_t table_width, int32_t* lengths, int advance,
+                             const float* inv_freq, int64_t batch, int64_t heads,
+                             int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                             int64_t block_size, int dtype, void* stream) {
+  if (!(batch > 0 && heads > 0 && kv_heads > 0 && head_dim > 0))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid q/k/v shapes");
+  if (head_dim % 2)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "head_dim must be even for rotate-half RoPE");
+  if (!(num_blocks > 0 && block_size > 0))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid cache shape");
+  if (table_width <= 0) return fail(PDB_ERR_INVALID_ARGUMENT, "invalid table width");
+  if (dtype != PDB_DTYPE_FLOAT32 && dtype != PDB_DTYPE_FLOAT16)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "use FP32 or FP16");
+  if (batch > INT32_MAX || heads * head_dim > INT32_MAX || kv_heads * head_dim > INT32_MAX ||
+      table_width * block_size > INT32_MAX)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "shape too large");
+  if (!q || !k || !v || !q_out || !k_out || !k_pool || !v_pool || !tables || !lengths ||
+      !inv_freq)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  pdb::RopeParams p{};
+  p.q = q; p.k = k; p.v = v; p.q_out = q_out; p.k_out = k_out;
+  p.k_pool = k_pool; p.v_pool = v_pool;
+  p.inv_freq = inv_freq;
+  p.seq = 1;
+  p.heads = (int)heads; p.kv_heads = (int)kv_heads; p.dim = (int)head_dim;
+  p.num_blocks = num_blocks; p.block_size = (int)block_size;
+  p.num_rows = batch;
+  p.tables = tables; p.table_width = table_width; p.lengths = lengths;
+  p.advance = advance ? 1 : 0;
+  return launch_rope(p, dtype, static_cast<cudaStream_t>(stream));
 }
 
 int pdb_read_device_errors(uint32_t* flags, int clear) {

@@ -97,7 +97,65 @@ struct RopeParams {
   int64_t num_blocks;
   int block_size;
   int64_t num_rows;
+  // Decode with device-resident metadata (tables != NULL, seq == 1): row b's
+  // position and slot come from lengths[b] and its table row, see
+  // resolve_row; positions / physical / offsets are unused.
+  const int32_t* tables;
+  int64_t table_width;
+  int32_t* lengths;
+  int advance;
 };
+
+// Position of row r and the element offset of its pool slot (-1: no write).
+// Given metadata: L = lengths[r]; the new token's position is L when the
+// call advances the lengths (the first layer of a decode step, where
+// lengths[r] then becomes L + 1, as PagedLlama.decode does with its host
+// lengths, worker/llama.py:154-158), else L - 1 (later layers, lengths
+// already count the token); its slot is (tables[r][pos / bs], pos % bs)
+// (TensorPagedKV.slots, worker/llama.py:40-47). A length or position
+// outside the table raises PDB_DEVERR_LENGTH, a page outside the pool
+// PDB_DEVERR_TABLE_ENTRY; the row's write is then skipped.
+// Without metadata: positions / physical / offsets / slot_of_row as given.
+__device__ __forceinline__ void resolve_row(const RopeParams& p, int64_t r, int64_t* pos_out,
+                                            long long* base_out, int* len_out) {
+  long long base = -1;
+  int64_t pos = 0;
+  if (p.tables) {
+    const int L = p.lengths[r];
+    *len_out = L;
+    pos = p.advance ? (int64_t)L : (int64_t)L - 1;
+    const int64_t cap = p.table_width * p.block_size;
+    if (L < 0 || pos < 0 || pos >= cap) {
+      raise_error(0x2u);
+      pos = pos < 0 ? 0 : (pos >= cap ? cap - 1 : pos);
+    } else {
+      const int page = p.tables[r * p.table_width + pos / p.block_size];
+      if (page < 0 || (int64_t)page >= p.num_blocks) {
+        raise_error(0x1u);
+      } else {
+        base = ((int64_t)page * p.block_size + pos % p.block_size) * p.kv_heads * p.dim;
+      }
+    }
+  } else {
+    const int64_t bi = r / p.seq, si = r - bi * p.seq;
+    pos = p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
+    const int64_t slot = p.slot_of_row ? (int64_t)p.slot_of_row[r] : r;
+    if (slot >= 0) {
+      if (slot < p.num_slots) {
+        const int64_t phys = p.physical[slot], off = p.offsets[slot];
+        if (phys < 0 || phys >= p.num_blocks || off < 0 || off >= p.block_size) {
+          raise_error(0x4u);
+        } else {
+          base = (phys * p.block_size + off) * p.kv_heads * p.dim;
+        }
+      } else {
+        raise_error(0x8u);
+      }
+    }
+  }
+  *pos_out = pos;
+  *base_out = base;
+}
 
 // cos and sin of an fp32 angle, as fp32 values destined for dtype T.
 // sincosf is within 2 fp32 ulps. For FP16 the result is then rounded to 11
@@ -141,11 +199,20 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
   grid_dependency_wait();
   launch_dependents();
   extern __shared__ float cs[];  // [2][dim/2]
+  __shared__ long long row_pos, row_base;
   const int64_t r = blockIdx.x;
   const int half = p.dim >> 1;
-  const int64_t bi = r / p.seq, si = r % p.seq;
-  const int64_t pos = p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
-  const float fpos = (float)pos;  // positions.float(): round-to-nearest
+  if (threadIdx.x == 0) {
+    int64_t pos;
+    long long base;
+    int len = 0;
+    resolve_row(p, r, &pos, &base, &len);
+    row_pos = pos;
+    row_base = base;
+    if (p.tables && p.advance) p.lengths[r] = len + 1;  // only this thread reads it
+  }
+  __syncthreads();
+  const float fpos = (float)row_pos;  // positions.float(): round-to-nearest
   for (int j = threadIdx.x; j < half; j += blockDim.x) {
     const float ang = __fmul_rn(fpos, p.inv_freq[j]);
     float c, s;
@@ -155,21 +222,7 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
   }
   __syncthreads();
 
-  // Destination slot of this row (or none).
-  int64_t slot = p.slot_of_row ? (int64_t)p.slot_of_row[r] : r;
-  int64_t phys = -1, off = 0;
-  if (slot >= 0) {
-    if (slot < p.num_slots) {
-      phys = p.physical[slot];
-      off = p.offsets[slot];
-      if (phys < 0 || phys >= p.num_blocks || off < 0 || off >= p.block_size) {
-        if (threadIdx.x == 0) raise_error(0x4u);
-        phys = -1;
-      }
-    } else {
-      if (threadIdx.x == 0) raise_error(0x8u);
-    }
-  }
+  const long long base = row_base;  // destination slot of this row (or none)
 
   const T* q = static_cast<const T*>(p.q) + r * p.heads * p.dim;
   T* qo = static_cast<T*>(p.q_out) + r * p.heads * p.dim;
@@ -185,8 +238,7 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
   const T* v = static_cast<const T*>(p.v) + kv_row;
   T* kslot = nullptr;
   T* vslot = nullptr;
-  if (phys >= 0) {
-    const int64_t base = (phys * p.block_size + off) * p.kv_heads * p.dim;
+  if (base >= 0) {
     kslot = static_cast<T*>(p.k_pool) + base;
     vslot = static_cast<T*>(p.v_pool) + base;
   }
@@ -231,40 +283,33 @@ __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
   constexpr int VEC = 16 / (int)sizeof(T);
   extern __shared__ float cs[];  // [ROWS][2][dim/2]
   __shared__ long long slot_base[ROWS];
+  __shared__ float row_fpos[ROWS];
   const int half = p.dim >> 1;
   const int hchunks = half / VEC;  // chunks per half-row of one head
   const int64_t r0 = (int64_t)blockIdx.x * ROWS;
 
+  if (threadIdx.x < ROWS) {
+    const int64_t r = r0 + threadIdx.x;
+    long long base = -1;
+    int64_t pos = 0;
+    if (r < p.num_rows) {
+      int len = 0;
+      resolve_row(p, r, &pos, &base, &len);
+      if (p.tables && p.advance) p.lengths[r] = len + 1;  // only this thread reads it
+    }
+    slot_base[threadIdx.x] = base;
+    row_fpos[threadIdx.x] = (float)pos;  // positions.float(): round-to-nearest
+  }
+  __syncthreads();
   for (int i = threadIdx.x; i < ROWS * half; i += blockDim.x) {
     const int rr = i / half, j = i - rr * half;
     const int64_t r = r0 + rr;
     if (r >= p.num_rows) continue;
-    const int64_t bi = r / p.seq, si = r - bi * p.seq;
-    const float fpos = (float)p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
+    const float fpos = row_fpos[rr];
     float c, s;
     rope_cos_sin<T>(__fmul_rn(fpos, p.inv_freq[j]), &c, &s);
     cs[(rr * 2) * half + j] = Elem<T>::to_f(Elem<T>::from_f(c));
     cs[(rr * 2 + 1) * half + j] = Elem<T>::to_f(Elem<T>::from_f(s));
-  }
-  if (threadIdx.x < ROWS) {
-    const int64_t r = r0 + threadIdx.x;
-    long long base = -1;
-    if (r < p.num_rows) {
-      const int64_t slot = p.slot_of_row ? (int64_t)p.slot_of_row[r] : r;
-      if (slot >= 0) {
-        if (slot < p.num_slots) {
-          const int64_t phys = p.physical[slot], off = p.offsets[slot];
-          if (phys < 0 || phys >= p.num_blocks || off < 0 || off >= p.block_size) {
-            raise_error(0x4u);
-          } else {
-            base = (phys * p.block_size + off) * p.kv_heads * p.dim;
-          }
-        } else {
-          raise_error(0x8u);
-        }
-      }
-    }
-    slot_base[threadIdx.x] = base;
   }
   __syncthreads();
 

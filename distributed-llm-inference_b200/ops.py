@@ -29,8 +29,8 @@ def _check(cond: bool, msg: str) -> None:
 
 # --------------------------------------------------------------------------
 # Workspace cache: one grow-only buffer per (device, stream, op). Calls on one
-# stream are ordered, so calls of the same op can share it; the buffer
-# never needs clearing (each call clears the counters it uses).
+# stream are ordered, so calls of the same op can share it; the buffer never
+# needs clearing (counters carry a per-call tag, so stale bytes count as zero).
 # --------------------------------------------------------------------------
 _ws_lock = threading.Lock()
 _ws_cache: dict[tuple[int, int, str], torch.Tensor] = {}
@@ -199,6 +199,67 @@ def rope_kv_write(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: tor
     _lib.check(rc, "rope_kv_write")
     if squeeze:
         return q_out.squeeze(1), k_out.squeeze(1)
+    return q_out, k_out
+
+
+def rope_kv_write_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                         k_pool: torch.Tensor, v_pool: torch.Tensor, tables: torch.Tensor,
+                         lengths: torch.Tensor, inv_freq: torch.Tensor, *,
+                         advance: bool = False, inplace: bool = False,
+                         q_out: torch.Tensor | None = None, k_out: torch.Tensor | None = None):
+    """Decode prologue driven by device-resident metadata.
+
+    The RoPE + KV-slot write of ``rope_kv_write`` for one new token per
+    sequence, with each token's position and slot derived on the GPU from the
+    batch's int32 block ``tables`` [B, W] and int32 ``lengths`` [B] instead of
+    host-computed positions and slots (TensorPagedKV.slots/metadata and the
+    bookkeeping of PagedLlama.decode, worker/llama.py:40-55, :154-159). With
+    ``advance`` the position is ``lengths[b]`` and ``lengths`` is incremented
+    in place (the first layer of a step); otherwise the position is
+    ``lengths[b] - 1``. q [B, H, D] or [B, 1, H, D]; k, v [B, KVH, D] or
+    [B, 1, KVH, D]. Returns the rotated (q, k) as ``rope_kv_write`` does.
+    """
+    _check(q.is_cuda, "query must be on CUDA")
+    squeeze = q.dim() == 3
+    if not squeeze:
+        _check(q.dim() == 4 and q.size(1) == 1 and k.dim() == 4 and k.size(1) == 1,
+               "decode takes one token per sequence")
+        q, k, v = q.squeeze(1), k.squeeze(1), v.squeeze(1)
+    _check(q.dim() == 3 and k.dim() == 3 and k.shape == v.shape, "invalid Q/K/V shapes")
+    _check(k_pool.dim() == 4 and k_pool.shape == v_pool.shape, "invalid cache shape")
+    B, H, D = q.shape
+    KVH = k.size(1)
+    _check(k.size(0) == B and k.size(2) == D, "invalid Q/K/V shapes")
+    _check(k_pool.size(2) == KVH and k_pool.size(3) == D, "invalid cache shape")
+    _check(q.dtype in _DTYPES, "use FP32 or FP16")
+    for t in (k, v, k_pool, v_pool):
+        _check(t.dtype == q.dtype, "dtype mismatch")
+    for t in (q, k, v, k_pool, v_pool, tables, lengths, inv_freq):
+        _check(t.device == q.device, "all tensors must be on the same GPU")
+        _check(t.is_contiguous(), "all tensors must be contiguous")
+    _check(tables.dtype == torch.int32 and lengths.dtype == torch.int32,
+           "tables and lengths must be int32")
+    _check(tables.dim() == 2 and tables.size(0) == B and tables.size(1) > 0,
+           "tables must be [batch, width]")
+    _check(lengths.dim() == 1 and lengths.size(0) == B, "lengths must be [batch]")
+    _check(inv_freq.dtype == torch.float32 and inv_freq.numel() == D // 2, "invalid inv_freq")
+    lib = _lib.load()
+    if q_out is not None or k_out is not None:
+        _check(q_out is not None and k_out is not None, "give both q_out and k_out")
+        q_out, k_out = q_out.view(q.shape), k_out.view(k.shape)
+        _check(q_out.dtype == q.dtype and k_out.dtype == q.dtype and q_out.is_contiguous()
+               and k_out.is_contiguous() and q_out.device == q.device
+               and k_out.device == q.device, "invalid outputs")
+    else:
+        q_out = q if inplace else torch.empty_like(q)
+        k_out = k if inplace else torch.empty_like(k)
+    with _DeviceGuard(q.device):
+        rc = lib.pdb_rope_kv_write_decode(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), q_out.data_ptr(), k_out.data_ptr(),
+            k_pool.data_ptr(), v_pool.data_ptr(), tables.data_ptr(), tables.size(1),
+            lengths.data_ptr(), 1 if advance else 0, inv_freq.data_ptr(), B, H, KVH, D,
+            k_pool.size(0), k_pool.size(1), _DTYPES[q.dtype], _stream_ptr(q.device))
+    _lib.check(rc, "rope_kv_write_decode")
     return q_out, k_out
 
 

@@ -192,6 +192,37 @@ PDB_API size_t pdb_rope_kv_write_workspace_size(int64_t batch, int64_t seq,
                                         int has_valid);
 
 /*
+ * Decode prologue with the batch's metadata resident on the device: the
+ * RoPE + KV-slot write of pdb_rope_kv_write for one new token per sequence,
+ * its positions and slots derived on the device instead of computed on the
+ * host and copied in every step.
+ * Replaces: the host slot and position computation of a decode step
+ *           (TensorPagedKV.slots / .metadata, worker/llama.py:40-55; the
+ *           position, slot and length bookkeeping of PagedLlama.decode,
+ *           worker/llama.py:154-159) together with its RoPE + slot writes
+ *           (worker/llama.py:168-172).
+ *   q, q_out [batch, heads, head_dim]; k, k_out, v [batch, kv_heads, head_dim]
+ *   tables   int32 [batch, table_width], row b = sequence b's pages (padding
+ *            beyond its pages is never read)
+ *   lengths  int32 [batch], sequence b's cached tokens
+ *   advance  nonzero: the new token's position is lengths[b] and the call
+ *            sets lengths[b] += 1 (the first layer of a step, as
+ *            PagedLlama.decode increments its lengths before attention);
+ *            zero: the position is lengths[b] - 1 (later layers)
+ * Sequence b's token goes to slot (tables[b][pos / block_size],
+ * pos % block_size) of k_pool / v_pool. A length or position outside the
+ * table, or a page outside the pool, skips the row's write and sets a
+ * device error bit (pdb_read_device_errors). No workspace; capturable.
+ */
+PDB_API int pdb_rope_kv_write_decode(const void* q, const void* k, const void* v, void* q_out,
+                                     void* k_out, void* k_pool, void* v_pool,
+                                     const int32_t* tables, int64_t table_width,
+                                     int32_t* lengths, int advance, const float* inv_freq,
+                                     int64_t batch, int64_t heads, int64_t kv_heads,
+                                     int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                     int dtype, void* stream);
+
+/*
  * Reads (and optionally clears) the error word of the current device.
  * Synchronises the device. No reference counterpart: the reference kernel
  * does not validate table entries or lengths on the device.

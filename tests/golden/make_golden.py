@@ -189,6 +189,26 @@ def main(ref_root: str) -> None:
     fixtures["scalar"] = dict(q=[1., 2.], keys=keys, values=vals, block_size=2,
                               table=kv.tables["a"], out=kv.attention("a", [1., 2.]))
     torch.save(fixtures, HERE / "scalar_known_answer.pt")
+
+    # 7. The reference's own PagedLlama (worker/llama.py:89-177, torch attention)
+    #    on a seeded random-init tiny Llama, driven through the serving
+    #    scenario (prefill, decode, release, re-admit on reused pages), CPU FP32.
+    #    transformers 5 moved rope_theta into rope_parameters and reports a
+    #    default rope_scaling; the two-line shim restores the 4.x view the
+    #    reference reads (worker/llama.py:94, :105).
+    from oracle import llama_model as LM
+    cfg = LM.tiny_llama_config()
+    model = LM.seeded_model(cfg, seed=1234)
+    cfg.rope_theta = LM.rope_theta(cfg)
+    cfg.rope_scaling = None
+    runner = PagedLlama(model, None, blocks=64, block_size=16, attention="torch")
+    steps = LM.scenario(seed=7, vocab=cfg.vocab_size)
+    logits = LM.run_scenario(runner, steps)
+    torch.save(dict(seed=1234, blocks=64, block_size=16, steps=steps, logits=logits,
+                    weights_checksum=LM.weights_checksum(model),
+                    k_pool_digest=digest(runner.cache.keys),
+                    v_pool_digest=digest(runner.cache.values)),
+               HERE / "llama_tiny_scenario.pt")
     print("wrote", sorted(p.name for p in HERE.glob("*.pt")))
 
 
