@@ -15,6 +15,16 @@ than L2, so no flush is needed between steps.
   python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU)
 
+Second workload, ``--workload smollm_tick``: one decode tick of a random-init
+SmolLM2-135M architecture (FP16, 30 layers, 9/3 heads, head_dim 64) for 128
+sequences with lengths U[16, 4096] on pages reused in arbitrary order; the
+whole model runs (embedding, projections, MLP, LM head in PyTorch/cuBLAS;
+RoPE, KV writes, metadata and attention on this library), one replica per
+GPU. Ours: llama_runner.PagedLlama with graph-captured ticks. Reference arm:
+the reference's PagedLlama.decode (restated in oracle/llama_model.py, pinned
+to its logits) with the reference's own CUDA attention kernel when it was
+built into oracle/_ref, else its torch path.
+
 Prints one JSON line (rank 0).
 """
 from __future__ import annotations
@@ -46,7 +56,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16"], default="llama3_8b")
+    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16", "smollm_tick"],
+                    default="llama3_8b")
     ap.add_argument("--batch", type=int, default=None, help="override the workload batch")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling)")
     ap.add_argument("--sharding", choices=["balanced", "contiguous"], default="balanced",
@@ -535,9 +546,198 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------
+# decode tick of the SmolLM2-135M architecture (the model runner)
+# --------------------------------------------------------------------------
+TICK_METRIC = "decode tokens/s (SmolLM2-135M arch, 128 sequences, len U[16,4096])"
+TICK_UNIT = "tokens/s"
+TICK_SEED_MODEL, TICK_SEED_STATE = 2024, 5
+
+
+def _tick_common(args):
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    if args.steps + max(args.warmup, 3) > 200:
+        raise SystemExit("smollm_tick: steps + warmup must stay within the 256 reserved tokens")
+    B = args.batch or 128
+    cfg = W.smollm2_135m_config()
+    model = W.seeded_llama(cfg, TICK_SEED_MODEL, torch.float16, device)
+    blocks = W.tick_blocks(B, TICK_SEED_STATE)
+    g = torch.Generator().manual_seed(99)
+    toks = torch.randint(0, cfg.vocab_size, (args.warmup + 2 * args.steps + 4, B), generator=g)
+    return world, rank, device, B, cfg, model, blocks, toks
+
+
+def _tick_bytes(cfg, lengths, model) -> float:
+    """Algorithmic HBM bytes of one tick: every weight once, every cached K/V
+    row of every layer once (2 * len * kv_heads * head_dim * 2 bytes)."""
+    weights = sum(p.numel() for p in model.parameters()) * 2
+    kv = 2 * float(lengths.sum()) * cfg.num_key_value_heads * cfg.head_dim * 2
+    return weights + kv * cfg.num_hidden_layers
+
+
+def _tick_e2e(runner, ids, toks, start, steps, device):
+    """``steps`` ticks through the public API: token ids in (H2D), greedy next
+    token out (D2H), CUDA events on the current stream; returns ms per tick."""
+    nxt = toks[start].tolist()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        logits = runner.decode(ids, nxt)
+        nxt = logits.argmax(-1).tolist()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_tick(args):
+    world, rank, device, B, cfg, model, blocks, toks = _tick_common(args)
+    runner = PKG.PagedLlama(model, None, blocks=blocks, block_size=16, max_batch=B, graphs=True)
+    ids, lengths = W.decode_tick_state(runner.cache, B, TICK_SEED_STATE)
+    for i in range(max(args.warmup, 3)):  # eager tick, capture, replays
+        runner.decode(ids, toks[i].tolist())
+    torch.cuda.synchronize(device)
+    tick = runner._b200_graphs[B]
+    with torch.inference_mode():  # the graph's buffers were made in inference mode
+        tick.tokens.copy_(toks[0].view(B, 1))
+    # device time: the captured tick replayed back to back (inputs resident)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    barrier(world, device)
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        tick.graph.replay()
+    e1.record()
+    e1.synchronize()
+    clk = clocks.stop()
+    ms_tick = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
+    # the replays advanced the device lengths past the host's: re-upload them
+    runner.cache._rows = [None] * runner.cache.max_batch
+    barrier(world, device)
+    ms_e2e = max_over_ranks(_tick_e2e(runner, ids, toks, max(args.warmup, 3), args.steps,
+                                      device), world, device)
+    ms_attn = _time_attention_share(runner, B, device)
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
+        REPO / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs") or 6650.0
+    nbytes = _tick_bytes(cfg, lengths + max(args.warmup, 3), model)
+    if rank == 0:
+        line = {
+            "metric": TICK_METRIC, "value": world * B / (ms_tick * 1e-3), "unit": TICK_UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": ms_tick, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded random-init weights and KV; no checkpoint)",
+            "config": {"workload": "smollm2-135m decode tick: 30 layers, 9/3 heads, head_dim 64, "
+                                   f"hidden 576, vocab 49152, batch {B} per GPU, lengths "
+                                   "U[16,4096], pages reused in shuffled order, block 16",
+                       "batch_per_gpu": B, "mean_length": float(lengths.float().mean()),
+                       "parallelism": f"replica x{world}",
+                       "step": "one CUDA graph per tick: embedding, 30 x (norm, q/k/v proj, "
+                               "rope_kv_write_decode, paged_attention, o proj, MLP), norm, "
+                               "LM head",
+                       "l2": "inputs larger than L2 (KV %.1f GB)" % (
+                           2 * runner.cache.keys.numel() * 2 / 1e9)},
+            "roofline": {"bound": "hbm", "achieved": nbytes / (ms_tick * 1e-3) / 1e9,
+                         "peak": peak, "unit": "GB/s",
+                         "frac": nbytes / (ms_tick * 1e-3) / 1e9 / peak, "traffic": None,
+                         "kernel": "whole tick (weights once + every cached K/V row once)",
+                         "algorithmic_bytes_per_step": nbytes,
+                         "attention_ms_per_step": ms_attn},
+            "clocks": clk,
+            "gpu_launches": args.steps * cfg.num_hidden_layers * 2,
+            "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": TICK_UNIT,
+                    "ms_per_step": ms_e2e, "h2d_bytes_per_step": B * 8,
+                    "d2h_bytes_per_step": B * 8,
+                    "path": "PagedLlama.decode(ids, tokens) per tick, greedy next token to "
+                            "the host"},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[device.index])
+        dist.destroy_process_group()
+
+
+def _time_attention_share(runner, B, device, reps=10):
+    """Attention launches of one tick alone (same pools, tables and lengths)."""
+    cache = runner.cache
+    q = torch.randn(B, runner.heads, runner.head_dim, device=device, dtype=runner.dtype)
+    tables, lengths = cache.dev_tables[:B], cache.dev_lengths[:B]
+    out = torch.empty_like(q)
+    layers = cache.keys.size(0)
+
+    def run():
+        for i in range(layers):
+            PKG.paged_attention(q, cache.keys[i], cache.values[i], tables, lengths,
+                                cache.max_tokens, out=out)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        run()
+    torch.cuda.synchronize(device)
+    g = capture(run, stream)
+    return time_graph(g, reps, stream) / reps
+
+
+def run_tick_reference(args):
+    """The reference decode tick (worker/llama.py:151-177, restated and pinned
+    in oracle/llama_model.py) with its own CUDA attention kernel (or its torch
+    path when that kernel was not built), same model, state and loop."""
+    world, rank, device, B, cfg, model, blocks, toks = _tick_common(args)
+    from oracle import build_ref
+    from oracle import llama_model as LM
+    mod = build_ref.load_ref_module()
+    if mod is not None:
+        def attention(q, k, v, tables, lengths, max_length):
+            return mod.paged_attention(q.contiguous(), k, v, tables.contiguous(),
+                                       lengths.contiguous(), max_length)
+        which = "reference CUDA kernel (cuda/paged_attention.cu, built into oracle/_ref)"
+    else:
+        attention, which = None, "reference torch path (torch_paged_attention)"
+    runner = LM.PagedLlamaOracle(model, blocks=blocks, block_size=16, attention=attention)
+    ids, lengths = W.decode_tick_state(runner.cache, B, TICK_SEED_STATE)
+    for i in range(max(args.warmup, 3)):
+        runner.decode(ids, toks[i].tolist())
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    barrier(world, device)
+    ms = max_over_ranks(_tick_e2e(runner, ids, toks, max(args.warmup, 3), args.steps, device),
+                        world, device)
+    clk = clocks.stop()
+    if rank == 0:
+        value = world * B / (ms * 1e-3)
+        print(json.dumps({
+            "metric": TICK_METRIC, "value": value, "unit": TICK_UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded random-init weights and KV; no checkpoint)",
+            "impl": "reference",
+            "config": {"workload": "smollm2-135m decode tick", "batch_per_gpu": B,
+                       "attention": which, "parallelism": f"replica x{world}"},
+            "clocks": clk,
+            "e2e": {"value": value, "unit": TICK_UNIT, "ms_per_step": ms,
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[device.index])
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.workload == "smollm_tick":
+        (run_tick_reference if args.impl == "reference" else run_tick)(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

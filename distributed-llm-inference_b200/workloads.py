@@ -303,3 +303,59 @@ def materialize_prefill(w: PrefillWorkload, device: torch.device | str) -> dict:
         "offsets": offs.to(device),
         "inv_freq": inv_freq(w.theta, w.head_dim).to(device),
     }
+
+
+# --------------------------------------------------------------------------
+# Decode tick of the SmolLM2-135M architecture (the model runner's workload)
+# --------------------------------------------------------------------------
+def smollm2_135m_config():
+    """SmolLM2-135M architecture: hidden 576, 30 layers, 9/3 heads, head_dim 64,
+    MLP 1536, RMSNorm eps 1e-5, vocab 49152, RoPE theta 1e5, tied embeddings."""
+    from transformers import LlamaConfig
+    return LlamaConfig(vocab_size=49152, hidden_size=576, intermediate_size=1536,
+                       num_hidden_layers=30, num_attention_heads=9, num_key_value_heads=3,
+                       head_dim=64, max_position_embeddings=8192, rms_norm_eps=1e-5,
+                       rope_theta=1e5, tie_word_embeddings=True)
+
+
+def seeded_llama(config, seed: int, dtype=torch.float16, device="cuda"):
+    """Random-init LlamaForCausalLM (no checkpoint here): initialised on the
+    CPU from ``seed``, then cast and moved; no gradients."""
+    from transformers import LlamaForCausalLM
+    torch.manual_seed(seed)
+    model = LlamaForCausalLM(config).eval()
+    for prm in model.parameters():
+        prm.requires_grad_(False)
+    return model.to(dtype=dtype, device=device)
+
+
+def tick_blocks(batch: int = 128, seed: int = 5, max_len: int = 4096, extra: int = 256,
+                block_size: int = 16) -> int:
+    """Pool blocks for decode_tick_state: 1.25 x the pages the batch reserves."""
+    g = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(16, max_len + 1, (batch,), generator=g)
+    pages = int(((lengths + extra + block_size - 1) // block_size).sum())
+    return math.ceil(1.25 * pages)
+
+
+def decode_tick_state(cache, batch: int = 128, seed: int = 5, max_len: int = 4096,
+                      extra: int = 256):
+    """Serving state of a decode tick on a TensorPagedKV-like ``cache``:
+    ``batch`` sequences with lengths U[16, max_len] (seeded), each holding the
+    pages for its length + ``extra`` tokens, taken from a shuffled free list
+    (pages freed and reused in arbitrary order, as after many requests), and
+    every pool byte set to seeded N(0, 1) values (the sequences' cached K/V
+    and the stale cells of freed pages alike). Returns (ids, lengths)."""
+    g = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(16, max_len + 1, (batch,), generator=g)
+    order = torch.randperm(len(cache.free), generator=g).tolist()
+    cache.free[:] = [cache.free[i] for i in order]
+    ids = [f"seq{i}" for i in range(batch)]
+    for rid, n in zip(ids, lengths.tolist()):
+        if not cache.reserve(rid, n + extra):
+            raise RuntimeError("pool too small for the tick workload")
+        cache.lengths[rid] = n
+    gen = torch.Generator(device=cache.keys.device).manual_seed(seed + 1)
+    for pool in (cache.keys, cache.values):
+        pool.normal_(0.0, 1.0, generator=gen)
+    return ids, lengths

@@ -29,8 +29,13 @@ def rope_theta(config) -> float:
 
 
 class PagedLlamaOracle:
-    def __init__(self, model, blocks: int = 256, block_size: int = 16):
+    """``attention`` plays the role of the reference's attention choice
+    (worker/llama.py:162): the torch path by default, or any function with
+    the paged_attention signature (e.g. the reference's own CUDA kernel)."""
+
+    def __init__(self, model, blocks: int = 256, block_size: int = 16, attention=None):
         self.model = model.eval()
+        self.attention_fn = attention or paged_attention
         self.config = model.config
         self.device = next(model.parameters()).device
         self.dtype = next(model.parameters()).dtype
@@ -100,8 +105,8 @@ class PagedLlamaOracle:
             q, k = rope(q, k, positions, self.inv_freq)
             self.cache.keys[index][slots] = k[:, 0]
             self.cache.values[index][slots] = v[:, 0]
-            context = paged_attention(q[:, 0], self.cache.keys[index], self.cache.values[index],
-                                      tables, lengths, max_length)
+            context = self.attention_fn(q[:, 0], self.cache.keys[index],
+                                        self.cache.values[index], tables, lengths, max_length)
             x = residual + attn.o_proj(context.reshape(batch, 1, -1))
             x = x + layer.mlp(layer.post_attention_layernorm(x))
         return self.model.lm_head(self.model.model.norm(x[:, 0])).float()
