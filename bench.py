@@ -25,6 +25,12 @@ the reference's PagedLlama.decode (restated in oracle/llama_model.py, pinned
 to its logits) with the reference's own CUDA attention kernel when it was
 built into oracle/_ref, else its torch path.
 
+Third workload, ``--workload prefill``: the prefill attention of 16 prompts
+with lengths U[64, 1024] (SmolLM2 heads 9/3, head_dim 64, FP16), one layer
+per step. Ours: prefill_attention over the paged pools. Reference arm: the
+reference's prefill attention (worker/llama.py:141-144: repeat_interleave
+of K/V and causal SDPA over the padded batch) on the same GPU.
+
 Prints one JSON line (rank 0).
 """
 from __future__ import annotations
@@ -56,7 +62,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16", "smollm_tick"],
+    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16", "smollm_tick", "prefill"],
                     default="llama3_8b")
     ap.add_argument("--batch", type=int, default=None, help="override the workload batch")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling)")
@@ -733,9 +739,101 @@ def run_tick_reference(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------
+# prefill attention (16 prompts, SmolLM2 heads)
+# --------------------------------------------------------------------------
+PREFILL_METRIC = "prefill attention prompt tokens/s per layer (16 prompts, len U[64,1024])"
+
+
+def _prefill_case(device, B=16, H=9, KVH=3, D=64, bs=16, seed=4):
+    g = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(64, 1025, (B,), generator=g)
+    Wd = int(lengths.max())
+    pages = ((lengths + bs - 1) // bs).tolist()
+    N = int(1.25 * sum(pages))
+    perm = torch.randperm(N, generator=g)
+    tables = torch.zeros(B, max(pages), dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(pages):
+        tables[b, :n] = perm[off:off + n].to(torch.int32)
+        off += n
+    q = torch.randn(B, Wd, H, D, generator=g).half().to(device)
+    k = torch.randn(B, Wd, KVH, D, generator=g).half().to(device)
+    v = torch.randn(B, Wd, KVH, D, generator=g).half().to(device)
+    valid = (torch.arange(Wd)[None, :] < lengths[:, None]).to(device)
+    tok = torch.arange(Wd)[None, :].expand(B, -1)
+    phys = tables.long().gather(1, (tok // bs).clamp(max=tables.shape[1] - 1)).to(device)
+    offs = (tok % bs).to(device)
+    k_pool = torch.randn(N, bs, KVH, D, generator=g).half().to(device)
+    v_pool = torch.randn(N, bs, KVH, D, generator=g).half().to(device)
+    k_pool[phys[valid], offs[valid]] = k[valid]
+    v_pool[phys[valid], offs[valid]] = v[valid]
+    flops = float(sum(n * (n + 1) // 2 for n in lengths.tolist())) * H * D * 4
+    return dict(q=q, k=k, v=v, k_pool=k_pool, v_pool=v_pool, tables=tables.to(device),
+                lengths=lengths.to(torch.int32).to(device), tokens=int(lengths.sum()),
+                flops=flops, H=H, KVH=KVH, D=D)
+
+
+def run_prefill(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    c = _prefill_case(device)
+    if args.impl == "reference":
+        import torch.nn.functional as F
+        groups = c["H"] // c["KVH"]
+
+        def step():  # worker/llama.py:141-144
+            ctx = F.scaled_dot_product_attention(
+                c["q"].transpose(1, 2), c["k"].repeat_interleave(groups, dim=2).transpose(1, 2),
+                c["v"].repeat_interleave(groups, dim=2).transpose(1, 2), is_causal=True)
+            return ctx.transpose(1, 2).reshape(c["q"].shape[0], c["q"].shape[1], -1)
+        which = "reference prefill attention: repeat_interleave + causal SDPA on the padded batch"
+    else:
+        out = torch.empty_like(c["q"])
+
+        def step():
+            return PKG.prefill_attention(c["q"], c["k_pool"], c["v_pool"], c["tables"],
+                                         c["lengths"], out=out)
+        which = "prefill_attention_kernel<64> (K/V from the paged pools)"
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize(device)
+    g = capture(step, stream)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    ms = time_graph(g, args.steps, stream) / args.steps
+    clk = clocks.stop()
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
+        REPO / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("bf16_tflops") or 1590.0
+    tflops = c["flops"] / (ms * 1e-3) / 1e12
+    line = {"metric": PREFILL_METRIC, "value": c["tokens"] / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic (seeded)",
+            "config": {"workload": "prefill attention: 16 prompts, len U[64,1024], heads 9/3, "
+                                   "head_dim 64, block 16, one layer per step",
+                       "kernel": which, "prompt_tokens": c["tokens"]},
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak,
+                         "unit": "TFLOP/s", "frac": tflops / peak, "traffic": None,
+                         "algorithmic_flops_per_step": c["flops"],
+                         "note": "causal FLOPs only (QK and PV over keys <= query)"},
+            "clocks": clk, "gpu_launches": args.steps if args.impl != "reference" else None}
+    if args.impl == "reference":
+        line["impl"] = "reference"
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
-    if args.workload == "smollm_tick":
+    if args.workload == "prefill":
+        run_prefill(args)
+    elif args.workload == "smollm_tick":
         (run_tick_reference if args.impl == "reference" else run_tick)(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -21,6 +21,7 @@
 #include "attention_tma.cuh"
 #include "attention_dyn.cuh"
 #include "rope_kv_write.cuh"
+#include "prefill.cuh"
 
 namespace {
 
@@ -729,6 +730,60 @@ int pdb_read_device_errors(uint32_t* flags, int clear) {
     if (e != cudaSuccess) return cuda_fail(e, "clear error word");
   }
   *flags = v;
+  return PDB_OK;
+}
+
+int pdb_prefill_attention(const void* q, const void* k_pool, const void* v_pool,
+                          const int32_t* tables, const int32_t* lengths, void* out,
+                          int64_t batch, int64_t width, int64_t heads, int64_t head_dim,
+                          int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                          int64_t table_width, int dtype, void* stream) {
+  if (dtype != PDB_DTYPE_FLOAT16)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "prefill attention takes FP16");
+  if (!(batch > 0 && width > 0 && heads > 0 && kv_heads > 0))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid q shape");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "prefill attention supports head_dim 64 and 128");
+  if (heads % kv_heads) return fail(PDB_ERR_INVALID_ARGUMENT, "query heads must be a multiple of KV heads");
+  if (!(num_blocks > 0 && block_size > 0 && table_width > 0))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid cache shape");
+  if (batch > 65535 || heads > 65535 || width > (int64_t)64 * 65535 || width > INT32_MAX / 2)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "shape too large");
+  if (!q || !k_pool || !v_pool || !tables || !lengths || !out)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  pdb::PrefillParams p{};
+  p.q = static_cast<const __half*>(q);
+  p.k_pool = static_cast<const __half*>(k_pool);
+  p.v_pool = static_cast<const __half*>(v_pool);
+  p.tables = tables;
+  p.lengths = lengths;
+  p.out = static_cast<__half*>(out);
+  p.B = (int)batch; p.W = (int)width; p.H = (int)heads; p.KVH = (int)kv_heads;
+  p.G = (int)(heads / kv_heads);
+  p.table_width = (int)table_width;
+  p.block_size = (int)block_size;
+  p.bs_shift = ((block_size & (block_size - 1)) == 0)
+                   ? __builtin_ctzll((unsigned long long)block_size) : -1;
+  p.num_blocks = num_blocks;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const void* fn = head_dim == 64 ? reinterpret_cast<const void*>(&pdb::prefill_attention_kernel<64>)
+                                  : reinterpret_cast<const void*>(&pdb::prefill_attention_kernel<128>);
+  const size_t smem = head_dim == 64 ? pdb::PrefillTile<64>::SMEM : pdb::PrefillTile<128>::SMEM;
+  if (ctas_per_sm(dev, fn, smem, 128) <= 0)
+    return fail(PDB_ERR_CUDA, "prefill attention kernel cannot be resident");
+  const dim3 grid((unsigned)((width + 63) / 64), (unsigned)heads, (unsigned)batch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == 64)
+    launch_pdl(pdb::prefill_attention_kernel<64>, grid, dim3(128), smem, st, p);
+  else
+    launch_pdl(pdb::prefill_attention_kernel<128>, grid, dim3(128), smem, st, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill attention launch");
   return PDB_OK;
 }
 

@@ -13,8 +13,10 @@ the cache access on this library's kernels:
   (embedding, every layer, final norm, LM head) is captured once per batch
   size as a CUDA graph and replayed; only the new token ids are copied in.
 * prefill (worker/llama.py:119-149): RoPE and the paged KV writes of every
-  prompt token in one ``rope_kv_write`` per layer (``valid`` mask), causal
-  SDPA over the padded prompts as in the reference.
+  prompt token in one ``rope_kv_write`` per layer (``valid`` mask), then the
+  causal attention from the pools (``prefill_attention``: no padding, no
+  repeated K/V) for FP16 with head_dim 64 or 128; other shapes use causal SDPA
+  over the padded prompts as the reference does.
 
 ``b200_decode`` / ``b200_prefill`` are the same methods as plain functions, so
 ``integration.install`` can put them on the reference's own class.
@@ -24,7 +26,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from .ops import paged_attention, rope_kv_write, rope_kv_write_decode
+from .ops import paged_attention, prefill_attention, rope_kv_write, rope_kv_write_decode
 from .paged_kv import DevicePagedKV
 
 
@@ -147,6 +149,9 @@ def b200_prefill(self, ids, token_lists):
     positions = torch.arange(width, device=self.device)[None, :].expand(batch, -1).contiguous()
     x = self.model.model.embed_tokens(tokens)
     groups = self.heads // self.kv_heads
+    paged = self.dtype == torch.float16 and self.head_dim in (64, 128)
+    if paged:
+        tables, lengths, _ = cache.metadata(ids)
     for index, layer in enumerate(self.model.model.layers):
         residual = x
         normalized = layer.input_layernorm(x)
@@ -157,10 +162,15 @@ def b200_prefill(self, ids, token_lists):
         q, k = rope_kv_write(q, k, v.contiguous(), cache.keys[index], cache.values[index],
                              physical, offsets, positions, self.inv_freq, valid=valid,
                              inplace=True)
-        context = F.scaled_dot_product_attention(
-            q.transpose(1, 2), k.repeat_interleave(groups, dim=2).transpose(1, 2),
-            v.repeat_interleave(groups, dim=2).transpose(1, 2), is_causal=True)
-        x = residual + attn.o_proj(context.transpose(1, 2).reshape(batch, width, -1))
+        if paged:
+            context = prefill_attention(q, cache.keys[index], cache.values[index], tables,
+                                        lengths)
+        else:
+            context = F.scaled_dot_product_attention(
+                q.transpose(1, 2), k.repeat_interleave(groups, dim=2).transpose(1, 2),
+                v.repeat_interleave(groups, dim=2).transpose(1, 2),
+                is_causal=True).transpose(1, 2)
+        x = residual + attn.o_proj(context.reshape(batch, width, -1))
         x = x + layer.mlp(layer.post_attention_layernorm(x))
     last = torch.tensor([len(s) - 1 for s in token_lists], device=self.device)
     hidden = self.model.model.norm(x[torch.arange(batch, device=self.device), last])

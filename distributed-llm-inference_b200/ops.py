@@ -263,6 +263,48 @@ def rope_kv_write_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return q_out, k_out
 
 
+def prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                      tables: torch.Tensor, lengths: torch.Tensor, *,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of a left-aligned prompt batch, K/V from the paged pools.
+
+    The prefill attention of worker/llama.py:141-144 (causal SDPA over the
+    padded batch with K/V repeated per query group) without the padding or
+    the repeat: q [B, W, H, D] FP16 (head_dim 64 or 128), pools
+    [blocks, bs, KVH, D] holding every prompt token's k/v (as rope_kv_write
+    leaves them), tables int32 [B, pages], lengths int32 [B]. Returns
+    [B, W, H, D]; rows at or beyond a prompt's length are zero.
+    """
+    _check(q.is_cuda, "query must be on CUDA")
+    for t in (q, k_pool, v_pool, tables, lengths):
+        _check(t.device == q.device, "all tensors must be on the same GPU")
+        _check(t.is_contiguous(), "all tensors must be contiguous")
+    _check(q.dim() == 4 and k_pool.dim() == 4 and k_pool.shape == v_pool.shape,
+           "invalid Q/K/V shapes")
+    B, Wd, H, D = q.shape
+    N, bs, KVH, Dk = k_pool.shape
+    _check(q.dtype == torch.float16 and k_pool.dtype == q.dtype and v_pool.dtype == q.dtype,
+           "prefill attention takes FP16")
+    _check(Dk == D and D in (64, 128), "prefill attention supports head_dim 64 and 128")
+    _check(H % KVH == 0, "query heads must be a multiple of KV heads")
+    _check(tables.dtype == torch.int32 and lengths.dtype == torch.int32, "metadata must be int32")
+    _check(tables.dim() == 2 and tables.size(0) == B, "invalid block tables")
+    _check(lengths.dim() == 1 and lengths.size(0) == B, "invalid lengths")
+    if out is None:
+        out = torch.empty_like(q)
+    else:
+        _check(out.shape == q.shape and out.dtype == q.dtype and out.is_contiguous()
+               and out.device == q.device, "invalid output tensor")
+    lib = _lib.load()
+    with _DeviceGuard(q.device):
+        rc = lib.pdb_prefill_attention(
+            q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), tables.data_ptr(),
+            lengths.data_ptr(), out.data_ptr(), B, Wd, H, D, N, bs, KVH, tables.size(1),
+            _lib.DTYPE_FLOAT16, _stream_ptr(q.device))
+    _lib.check(rc, "prefill_attention")
+    return out
+
+
 def read_device_errors(clear: bool = True) -> int:
     """Error bits raised by kernels on the current device (synchronises)."""
     import ctypes

@@ -239,6 +239,28 @@ PDB_API int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch,
                             int64_t kv_heads, int64_t grid, int64_t* ranges);
 
 /*
+ * Causal attention of a prefill batch, K/V read from the paged pools.
+ * Replaces: the prefill attention of worker/llama.py:141-144,
+ *   SDPA(q^T, repeat_interleave(k)^T, repeat_interleave(v)^T, is_causal=True)
+ * over left-aligned padded prompts.
+ *   q, out   FP16 [batch, width, heads, head_dim]   (head_dim 64 or 128)
+ *   k_pool, v_pool FP16 [num_blocks, block_size, kv_heads, head_dim], holding
+ *            every prompt token's (RoPE'd) k and v, as pdb_rope_kv_write leaves them
+ *   tables   int32 [batch, table_width], prompt b's pages in order
+ *   lengths  int32 [batch], prompt b's token count (<= width)
+ * Query t < lengths[b] of prompt b attends to keys 0..t of prompt b; rows
+ * t >= lengths[b] are written as zeros (no real row attends to them). Query
+ * head h reads kv head h / (heads / kv_heads). Out-of-range lengths or pages
+ * set device error bits (pdb_read_device_errors) and are clamped or skipped.
+ * No workspace; capturable.
+ */
+PDB_API int pdb_prefill_attention(const void* q, const void* k_pool, const void* v_pool,
+                                  const int32_t* tables, const int32_t* lengths, void* out,
+                                  int64_t batch, int64_t width, int64_t heads, int64_t head_dim,
+                                  int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                                  int64_t table_width, int dtype, void* stream);
+
+/*
  * Host-side copy of the default FP16 kernel's worker partition, for tests.
  * No reference counterpart. For `units` 16-token units and `launched` CTAs,
  * writes per worker w: ranges[3w], ranges[3w+1] = its [begin, end) and

@@ -68,3 +68,15 @@ def paged_attention_fp64(query, keys, values, tables, lengths) -> torch.Tensor:
             p = torch.softmax(s, dim=0)
             out[b, h] = p @ v[:, h // group]
     return out
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """worker/llama.py:141-144: causal SDPA over the padded prompt batch,
+    K/V repeated per query group. q [B, W, H, D], k/v [B, W, KVH, D];
+    returns [B, W, H, D] (computed in fp32)."""
+    groups = q.shape[2] // k.shape[2]
+    qf, kf, vf = q.float(), k.float(), v.float()
+    ctx = F.scaled_dot_product_attention(
+        qf.transpose(1, 2), kf.repeat_interleave(groups, dim=2).transpose(1, 2),
+        vf.repeat_interleave(groups, dim=2).transpose(1, 2), is_causal=True)
+    return ctx.transpose(1, 2)
