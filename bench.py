@@ -184,11 +184,24 @@ class DecodeStep:
     """All layers of one decode step through the public ops, with
     preallocated outputs so the step can be captured in a CUDA graph."""
 
-    def __init__(self, w, t):
+    def __init__(self, w, t, fused=True):
         self.w, self.t = w, t
         self.q_out = [torch.empty_like(q) for q in t.q]
         self.k_out = [torch.empty_like(k) for k in t.k]
         self.out = [torch.empty_like(q) for q in t.q]
+        # one launch per layer (decode_attention) where the fused kernel applies
+        self.fused = fused and PKG.decode_attention_supported(t.q[0], t.k_pools[0])
+
+    def layer(self, layer):
+        """RoPE + KV-slot write + attention of one layer (one or two launches)."""
+        t = self.t
+        if self.fused:
+            PKG.decode_attention(t.q[layer], t.k[layer], t.v[layer], t.k_pools[layer],
+                                 t.v_pools[layer], t.tables, t.lengths, t.inv_freq,
+                                 self.w.max_length, out=self.out[layer])
+        else:
+            self.prologue(layer)
+            self.attention(layer)
 
     def prologue(self, layer):
         t = self.t
@@ -203,8 +216,7 @@ class DecodeStep:
 
     def __call__(self):
         for layer in range(self.w.layers):
-            self.prologue(layer)
-            self.attention(layer)
+            self.layer(layer)
 
 
 def capture(fn, stream):
@@ -227,21 +239,26 @@ def time_graph(g, reps, stream):
 
 def e2e_run(w, t, steps, warmup, device):
     """Public-API path with host buffers: every step copies each layer's new
-    q/k/v (and the step's tables/lengths/positions/slots) from pinned host
-    memory, runs rope_kv_write + paged_attention, and copies each layer's
-    attention output back to pinned host memory. Copies of layer l+1 overlap
-    the kernels of layer l (separate copy streams, event ordering)."""
+    q/k/v (and the step's metadata: tables and lengths, plus positions and
+    slots for the two-launch path) from pinned host memory, runs
+    decode_attention (or rope_kv_write + paged_attention where the fused
+    kernel does not apply), and copies each layer's attention output back to
+    pinned host memory. Copies of layer l+1 overlap the kernels of layer l
+    (separate copy streams, event ordering)."""
     L = w.layers
+    fused = PKG.decode_attention_supported(t.q[0], t.k_pools[0])
     pin = lambda x: x.cpu().pin_memory()  # noqa: E731
     h_q = [pin(x) for x in t.q]
     h_k = [pin(x) for x in t.k]
     h_v = [pin(x) for x in t.v]
-    h_meta = [pin(x) for x in (t.tables, t.lengths, t.positions, t.physical, t.offsets)]
+    meta = (t.tables, t.lengths) if fused else (t.tables, t.lengths, t.positions, t.physical,
+                                                t.offsets)
+    h_meta = [pin(x) for x in meta]
     h_out = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in t.q]
     d_q = [torch.empty_like(x) for x in t.q]
     d_k = [torch.empty_like(x) for x in t.k]
     d_v = [torch.empty_like(x) for x in t.v]
-    d_meta = [torch.empty_like(x) for x in (t.tables, t.lengths, t.positions, t.physical, t.offsets)]
+    d_meta = [torch.empty_like(x) for x in meta]
     q_out = [torch.empty_like(x) for x in t.q]
     k_out = [torch.empty_like(x) for x in t.k]
     d_out = [torch.empty_like(x) for x in t.q]
@@ -265,14 +282,20 @@ def e2e_run(w, t, steps, warmup, device):
                 d_v[layer].copy_(h_v[layer], non_blocking=True)
                 copied[layer].record(h2d)
         comp.wait_event(copied[L])
-        tables, lengths, positions, physical, offsets = d_meta
+        tables, lengths = d_meta[0], d_meta[1]
         for layer in range(L):
             comp.wait_event(copied[layer])
-            PKG.rope_kv_write(d_q[layer], d_k[layer], d_v[layer], t.k_pools[layer],
-                              t.v_pools[layer], physical, offsets, positions, t.inv_freq,
-                              q_out=q_out[layer], k_out=k_out[layer])
-            PKG.paged_attention(q_out[layer], t.k_pools[layer], t.v_pools[layer], tables, lengths,
-                                w.max_length, out=d_out[layer])
+            if fused:
+                PKG.decode_attention(d_q[layer], d_k[layer], d_v[layer], t.k_pools[layer],
+                                     t.v_pools[layer], tables, lengths, t.inv_freq,
+                                     w.max_length, out=d_out[layer])
+            else:
+                positions, physical, offsets = d_meta[2:]
+                PKG.rope_kv_write(d_q[layer], d_k[layer], d_v[layer], t.k_pools[layer],
+                                  t.v_pools[layer], physical, offsets, positions, t.inv_freq,
+                                  q_out=q_out[layer], k_out=k_out[layer])
+                PKG.paged_attention(q_out[layer], t.k_pools[layer], t.v_pools[layer], tables,
+                                    lengths, w.max_length, out=d_out[layer])
             done[layer].record(comp)
             with torch.cuda.stream(d2h):
                 d2h.wait_event(done[layer])
@@ -367,8 +390,21 @@ def run_ours(args):
         step()
     torch.cuda.synchronize(device)
     g_step = capture(step, stream)
-    g_attn = capture(lambda: [step.attention(i) for i in range(w.layers)], stream)
-    g_pro = capture(lambda: [step.prologue(i) for i in range(w.layers)], stream)
+    # roofline graphs: the step's dominant launches alone (the fused layer
+    # launches, or the attention launches of the two-launch path), and the
+    # two-launch step itself for comparison
+    if step.fused:
+        g_attn = capture(lambda: [step.layer(i) for i in range(w.layers)], stream)
+        g_pro = None
+        step2 = DecodeStep(w, t, fused=False)
+        with torch.cuda.stream(stream):
+            step2()
+        torch.cuda.synchronize(device)
+        g_two = capture(step2, stream)
+    else:
+        g_attn = capture(lambda: [step.attention(i) for i in range(w.layers)], stream)
+        g_pro = capture(lambda: [step.prologue(i) for i in range(w.layers)], stream)
+        g_two = None
 
     clocks = ClockSampler(device.index)
     clocks.start()
@@ -388,8 +424,10 @@ def run_ours(args):
     # roofline of the dominant kernel: attention launches alone, same inputs
     reps = max(3, min(20, args.steps))
     ms_attn = time_graph(g_attn, reps, stream) / (reps * w.layers)
-    ms_pro = time_graph(g_pro, reps, stream) / (reps * w.layers)
-    attn_bytes = w.attention_bytes()
+    ms_pro = time_graph(g_pro, reps, stream) / (reps * w.layers) if g_pro is not None else None
+    ms_two = time_graph(g_two, reps, stream) / reps if g_two is not None else None
+    # the fused launch does the prologue's work too, so it is charged its bytes
+    attn_bytes = w.attention_bytes() + (w.prologue_bytes() if step.fused else 0)
     peaks = {}
     pk = REPO / "MEASURED_PEAKS.json"
     if pk.exists():
@@ -421,7 +459,7 @@ def run_ours(args):
     alt = None
     if world > 1 and not args.no_alt:
         alt_mode = "contiguous" if args.sharding == "balanced" else "balanced"
-        del g_step, g_attn, g_pro
+        del g_step, g_attn, g_pro, g_two
         wa = full.shard(rank, world, alt_mode)
         ta = W.materialize(wa, device)
         step_a = DecodeStep(wa, ta)
@@ -439,7 +477,7 @@ def run_ours(args):
         alt = {"sharding": alt_mode, "value": full.batch / (ms_alt * 1e-3), "ms_per_step": ms_alt,
                "max_rank_tokens": max_over_ranks(float(wa.lengths.sum()), world, device)}
         del g_alt, step_a, ta
-        g_step = g_attn = g_pro = None
+        g_step = g_attn = g_pro = g_two = None
 
     # output checksum across ranks (outside every timed region)
     chk = torch.tensor([float(sum(o.float().abs().sum() for o in step.out))], device=device,
@@ -475,17 +513,21 @@ def run_ours(args):
                 "l2": "inputs larger than L2 (KV pools %.1f GB per rank)" % (
                     2 * w.layers * w.num_blocks * w.block_size * w.kv_heads * w.head_dim
                     * w.elem_bytes / 1e9),
-                "step": "per layer: rope_kv_write + paged_attention, one CUDA graph per step",
+                "step": ("per layer: decode_attention (RoPE + KV-slot write + attention in one "
+                         "launch), one CUDA graph per step" if step.fused else
+                         "per layer: rope_kv_write + paged_attention, one CUDA graph per step"),
             },
             "algorithmic_gb_per_step": full.seq_step_bytes() / 1e9,
             "achieved_gbs_step": full.seq_step_bytes() / (ms_step * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": ATTN_KERNEL, "peak_source": f"{peak_src} hbm_gbs",
+                         "kernel": ATTN_KERNEL if step.fused else ATTN_KERNEL_TWO,
+                         "peak_source": f"{peak_src} hbm_gbs",
                          "algorithmic_bytes_per_launch": attn_bytes,
-                         "ms_per_launch": ms_attn, "prologue_ms_per_launch": ms_pro},
+                         "ms_per_launch": ms_attn, "prologue_ms_per_launch": ms_pro,
+                         "two_launch_ms_per_step": ms_two},
             "clocks": clk,
-            "gpu_launches": args.steps * w.layers * 2,
+            "gpu_launches": args.steps * w.layers * (1 if step.fused else 2),
             "e2e": e2e,
             "cpu_baseline": base,
             "alt_sharding": alt,
@@ -499,9 +541,12 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# The kernel paged_attention launches for the FP16, head_dim 128, GQA-4 workload
-ATTN_KERNEL = ("attn_tma_dyn_kernel<MmaMath<128,4,3,TMA>>: TMA producer warp, tensor-core "
-               "stream-K, dynamic tail, epilogue warp")
+# The kernel a decode layer launches for the FP16, head_dim 128, GQA-4 workload
+ATTN_KERNEL = ("attn_tma_dyn_kernel<MmaMath<128,4,3,TMA>, fused prologue>: RoPE + KV-slot "
+               "write + attention, TMA producer warp, tensor-core stream-K, dynamic tail, "
+               "epilogue warp")
+ATTN_KERNEL_TWO = ("attn_tma_dyn_kernel<MmaMath<128,4,3,TMA>>: TMA producer warp, tensor-core "
+                   "stream-K, dynamic tail, epilogue warp")
 
 
 def run_reference(args):

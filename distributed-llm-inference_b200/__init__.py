@@ -7,6 +7,8 @@ Public ops (drop-in for the reference's decode path):
   rope_kv_write_decode(q, k, v, k_pool, v_pool, tables, lengths, inv_freq, advance=...)
       the decode prologue with positions and slots derived on the device
       (worker/llama.py:40-55, :154-159, :168-172)
+  decode_attention(q, k, v, k_pool, v_pool, tables, lengths, inv_freq, max_length)
+      one decode layer (RoPE, slot writes, attention) in one launch
   prefill_attention(q, k_pool, v_pool, tables, lengths)
       causal prefill attention with K/V from the pools (worker/llama.py:141-144)
   DevicePagedKV              TensorPagedKV (worker/llama.py:13-55) + device-resident
@@ -19,14 +21,16 @@ The package directory name contains '-', so import it with
 importlib.import_module("distributed-llm-inference_b200").
 """
 from ._lib import IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA, IMPL_TMA_STATIC, load as load_library  # noqa: F401
-from .ops import (fast_grid_size, paged_attention, prefill_attention,  # noqa: F401
-                  read_device_errors, rope_kv_write, rope_kv_write_decode)
+from .ops import (decode_attention, decode_attention_supported,  # noqa: F401
+                  fast_grid_size, paged_attention, prefill_attention, read_device_errors,
+                  rope_kv_write, rope_kv_write_decode)
 from .paged_kv import DevicePagedKV  # noqa: F401
 from .llama_runner import PagedLlama  # noqa: F401
 from .integration import cuda_paged_attention, install, uninstall  # noqa: F401
 
 __all__ = [
-    "paged_attention", "prefill_attention", "rope_kv_write", "rope_kv_write_decode",
+    "paged_attention", "decode_attention", "decode_attention_supported", "prefill_attention",
+    "rope_kv_write", "rope_kv_write_decode",
     "DevicePagedKV", "PagedLlama",
     "cuda_paged_attention", "install", "uninstall",
     "read_device_errors", "fast_grid_size", "load_library",

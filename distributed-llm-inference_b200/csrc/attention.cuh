@@ -62,6 +62,13 @@ struct AttnParams {
   unsigned long long call_tag;   // 48-bit salted tag of this call
   int splits;  // generic
   int chunk;   // generic: tokens per split
+  // Decode prologue folded into attn_tma_dyn_kernel<M, true> (else unused):
+  // q holds the un-rotated queries, rotated in the kernel at position
+  // lengths[b] - 1; k_new / v_new [B, KVH, D] hold the new token's k (not yet
+  // rotated) and v, which the kernel writes into the token's slot.
+  const void* k_new;
+  const void* v_new;
+  const float* inv_freq;
 };
 
 // Clamp a length read from device memory into [0, max_length].

@@ -37,6 +37,7 @@
 #pragma once
 
 #include "attention_tma.cuh"
+#include "rope_kv_write.cuh"
 
 namespace pdb {
 
@@ -235,10 +236,15 @@ struct TileRecord {
   long long w_first; // first worker of the segment
   long long w_last;  // last worker of the segment
   int first_slot;    // slot of the segment's piece in w_first
+  int len;           // tokens of sequence b (the fused prologue's position + 1)
+  int slot_row;      // fused, kRecNewRow tiles: pool row of the new token (-1: none)
   int pad;
 };
 // kRecOpen: the piece that starts here will not be a whole segment.
+// kRecNewTok (fused prologue): the piece that starts here contains the
+// segment's last unit, i.e. the new token; kRecNewRow: this tile holds it.
 constexpr int kRecFirst = 1, kRecLast = 2, kRecWhole = 4, kRecEnd = 8, kRecOpen = 16;
+constexpr int kRecNewTok = 32, kRecNewRow = 64;
 
 // Work queued by the math warps for the epilogue warp: the tag install of a
 // piece's counter when the piece starts, its arrival when it ends, the end.
@@ -254,6 +260,96 @@ constexpr int kHandArrive = 0, kHandInstall = 1, kHandEnd = 2;
 constexpr int kHandoffDepth = 8;
 constexpr int kDynMisc = 32;  // ints of per-CTA scratch
 
+// Fused decode prologue at the start of a piece (all math threads, tid <
+// NW * 32), in place of MmaMath::begin_piece: the lane's q elements and — for
+// the piece holding the new token — the token's k and v are loaded first, so
+// their latency overlaps the piece's cos/sin table (FP16-rounded, as
+// rope_kv_write computes them; inv_freq staged in shared memory); then q is
+// rotated into the lane's Q^T fragment (rotate-half: element i < D/2 pairs
+// with i + D/2) and the token's rotated k and its v go to `newrow`, from where
+// the tile holding the token is patched and the pool slot written. Per-op
+// FP16 rounding as in rope_kv_write. `sync` is a barrier over the math threads.
+template <class M, class Sync>
+__device__ __forceinline__ void fused_piece_start(typename M::State& st, const AttnParams& p,
+                                                  int b, int h, int pos, bool new_tok,
+                                                  const float* invf, float* cs, __half* newrow,
+                                                  Sync sync) {
+  constexpr int D = M::D, KS = M::KSTEPS, HALF = D / 2;
+  static_assert(KS % 2 == 0, "lower and upper halves in whole k-steps");
+  const int tid = threadIdx.x, lane = tid & 31, g = lane >> 2, tg = lane & 3;
+  const bool real = g < p.G;  // columns >= G are padding (q = 0)
+  const __half* qrow = static_cast<const __half*>(p.q) +
+                       ((int64_t)b * p.H + (int64_t)h * p.G + (real ? g : 0)) * D;
+  __half2 qx1[KS / 2][2], qx2[KS / 2][2];
+#pragma unroll
+  for (int ks = 0; ks < KS / 2; ++ks)
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int i = 16 * ks + 2 * tg + 8 * r;
+      qx1[ks][r] = *reinterpret_cast<const __half2*>(qrow + i);
+      qx2[ks][r] = *reinterpret_cast<const __half2*>(qrow + i + HALF);
+    }
+  __half k1 = __float2half_rn(0.f), k2 = k1, v1 = k1, v2 = k1;
+  const int64_t src = ((int64_t)b * p.KVH + h) * D;
+  if (new_tok && tid < HALF) {
+    k1 = static_cast<const __half*>(p.k_new)[src + tid];
+    k2 = static_cast<const __half*>(p.k_new)[src + tid + HALF];
+    v1 = static_cast<const __half*>(p.v_new)[src + tid];
+    v2 = static_cast<const __half*>(p.v_new)[src + tid + HALF];
+  }
+  if (tid < HALF) {
+    float c, s;
+    rope_cos_sin<__half>(__fmul_rn((float)pos, invf[tid]), &c, &s);
+    cs[tid] = __half2float(__float2half_rn(c));
+    cs[HALF + tid] = __half2float(__float2half_rn(s));
+  }
+  sync();
+  auto rot = [&](float x1, float x2, int i, __half* o1, __half* o2) {
+    const float c = cs[i], sn = cs[HALF + i];
+    const float a = __half2float(__float2half_rn(__fmul_rn(x1, c)));
+    const float bb = __half2float(__float2half_rn(__fmul_rn(x2, sn)));
+    const float d = __half2float(__float2half_rn(__fmul_rn(x2, c)));
+    const float e = __half2float(__float2half_rn(__fmul_rn(x1, sn)));
+    *o1 = __float2half_rn(__fsub_rn(a, bb));
+    *o2 = __float2half_rn(__fadd_rn(d, e));
+  };
+#pragma unroll
+  for (int ks = 0; ks < KS / 2; ++ks) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int i = 16 * ks + 2 * tg + 8 * r;  // elements i, i + 1 (lower half)
+      uint32_t lo = 0u, hi = 0u;
+      if (real) {
+        __half l0, h0, l1, h1;
+        rot(__low2float(qx1[ks][r]), __low2float(qx2[ks][r]), i, &l0, &h0);
+        rot(__high2float(qx1[ks][r]), __high2float(qx2[ks][r]), i + 1, &l1, &h1);
+        const __half2 lo2 = __halves2half2(l0, l1), hi2 = __halves2half2(h0, h1);
+        lo = *reinterpret_cast<const uint32_t*>(&lo2);
+        hi = *reinterpret_cast<const uint32_t*>(&hi2);
+      }
+      st.qb[ks][r] = lo;
+      st.qb[ks + KS / 2][r] = hi;
+    }
+  }
+  st.m[0] = st.m[1] = -INFINITY;
+  st.l[0] = st.l[1] = 0.f;
+#pragma unroll
+  for (int i = 0; i < KS; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) st.acc[i][j] = 0.f;
+  if (new_tok) {
+    if (tid < HALF) {
+      __half o1, o2;
+      rot(__half2float(k1), __half2float(k2), tid, &o1, &o2);
+      newrow[tid] = o1;
+      newrow[tid + HALF] = o2;
+      newrow[D + tid] = v1;
+      newrow[D + tid + HALF] = v2;
+    }
+    sync();
+  }
+}
+
 template <class M>
 struct DynStreamK {
   static_assert(M::LAYOUT == kTma128B, "dynamic kernel stages with TMA");
@@ -265,13 +361,17 @@ struct DynStreamK {
   static size_t smem_bytes(int B) {
     return 1024 + (size_t)STAGES * M::STAGE_BYTES + (size_t)MERGE_FLOATS * 4 +
            (size_t)(3 * B + 1 + kDynMisc) * 4 + (2 * STAGES + 2 * kHandoffDepth) * 8 + 16 +
-           (size_t)STAGES * sizeof(TileRecord) + kHandoffDepth * sizeof(PieceHandoff) + 16;
+           (size_t)STAGES * sizeof(TileRecord) + kHandoffDepth * sizeof(PieceHandoff) +
+           (size_t)D * 4 + (size_t)2 * D * 2 + (size_t)D / 2 * 4 +
+           64;  // + fused prologue: cos/sin, new row, inv_freq (+ alignment)
   }
   // partial slots: two per worker (static workers + tail chunks)
   static int64_t slots(int64_t launched) { return 2 * launched * (1 + kTailChunksPerCta); }
 };
 
-template <class M>
+// FUSE: the decode prologue (RoPE of q and of the new k, k/v slot writes) is
+// folded in; see AttnParams::k_new.
+template <class M, bool FUSE = false>
 __global__ void __launch_bounds__(DynStreamK<M>::NT, 2)
 attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     const __grid_constant__ CUtensorMap vmap) {
@@ -300,6 +400,13 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
   TileRecord* recs = reinterpret_cast<TileRecord*>(
       (reinterpret_cast<uintptr_t>(hf_empty + kHandoffDepth) + 15) & ~uintptr_t(15));
   PieceHandoff* hand = reinterpret_cast<PieceHandoff*>(recs + STAGES);
+  // fused prologue buffers, each 16-byte aligned (newrow is read as uint4)
+  auto align16 = [](const void* q) {
+    return (reinterpret_cast<uintptr_t>(q) + 15) & ~uintptr_t(15);
+  };
+  float* cs_tab = reinterpret_cast<float*>(align16(hand + kHandoffDepth));  // [2][D/2]
+  __half* newrow = reinterpret_cast<__half*>(align16(cs_tab + D));          // k[D], v[D]
+  float* invf = reinterpret_cast<float*>(align16(newrow + 2 * D));          // [D/2]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int KVH = p.KVH;
@@ -316,6 +423,9 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
   }
   launch_dependents();
   grid_dependency_wait();  // every global access comes after this
+  if constexpr (FUSE) {
+    for (int i = tid; i < D / 2; i += NT) invf[i] = __ldg(p.inv_freq + i);
+  }
   static_assert(3 + 3 * (NT / 32) <= kDynMisc, "plan scratch");
   DynPlan pl;
   const int64_t U = plan_dyn_stream<NT>(p, P, Ls, ord, misc, gridDim.x, TU, pl);
@@ -369,10 +479,13 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
           TileRecord r{};
           r.b = ord[c.b];
           r.h = c.h;
+          r.len = Ls[c.b];
           const int rem = Ls[c.b] - tok0;
           r.ntok = nunits * kUnitTokens < rem ? nunits * kUnitTokens : rem;
           r.flags = (piece_first ? kRecFirst : 0) | (last ? kRecLast : 0);
           if (piece_first && !(c.u == c.seg && c.seg + c.nu <= we)) r.flags |= kRecOpen;
+          if (FUSE && piece_first && c.seg + c.nu <= we) r.flags |= kRecNewTok;
+          if (FUSE && seg_end) r.flags |= kRecNewRow;
           if (last) {
             // The piece started at the worker's begin or at the segment's.
             const int64_t pstart = wb > c.seg ? wb : c.seg;
@@ -406,6 +519,16 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
           }
         }
         const unsigned okmask = __ballot_sync(0xffffffffu, ok);
+        if constexpr (FUSE) {
+          if (seg_end) {  // the new token sits in this tile's last unit
+            const int last = nunits - 1;
+            const int lrow = __shfl_sync(0xffffffffu, row0, last);
+            if (lane == 0)
+              recs[s].slot_row = ((okmask >> last) & 1u)
+                                     ? lrow + (Ls[c.b] - 1 - tok0 - last * kUnitTokens)
+                                     : -1;
+          }
+        }
         if (lane == 0) {
           fence_proxy_async_smem();
           mbar_arrive_expect_tx(&full[s], (uint32_t)__popc(okmask) * K::UNIT_BYTES);
@@ -501,6 +624,33 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
     unsigned char* sk = stage_k(s);
     unsigned char* sv = sk + M::TILE_BYTES;
     const int r0 = warp * M::WT;
+    if constexpr (FUSE) {
+      if (r.flags & kRecFirst)
+        fused_piece_start<M>(st, p, r.b, r.h, r.len - 1, (r.flags & kRecNewTok) != 0, invf,
+                             cs_tab, newrow, sync_math);
+      // The new token's row of this tile: the TMA brought the slot's old
+      // bytes; the owning warp writes the rotated k and the v in their place
+      // and into the pool slot (for later steps; this launch never reads the
+      // slot from global memory).
+      const int nr = r.ntok - 1;
+      if ((r.flags & kRecNewRow) && nr >= r0 && nr < r0 + M::WT) {
+        if (lane < D / 8) {
+          const uint4 kc = reinterpret_cast<const uint4*>(newrow)[lane];
+          const uint4 vc = reinterpret_cast<const uint4*>(newrow + D)[lane];
+          *reinterpret_cast<uint4*>(sk + M::offset(nr, lane)) = kc;
+          *reinterpret_cast<uint4*>(sv + M::offset(nr, lane)) = vc;
+          if (r.slot_row >= 0) {
+            const int64_t base = ((int64_t)r.slot_row * KVH + r.h) * D;
+            reinterpret_cast<uint4*>(static_cast<__half*>(const_cast<void*>(p.k_pool)) +
+                                     base)[lane] = kc;
+            reinterpret_cast<uint4*>(static_cast<__half*>(const_cast<void*>(p.v_pool)) +
+                                     base)[lane] = vc;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+    }
     if (r0 < r.ntok && r0 + M::WT > r.ntok) {
       for (int i = lane; i < (r0 + M::WT - r.ntok) * (D / 8); i += 32) {
         const int row = r.ntok + i / (D / 8), col = i % (D / 8);
@@ -511,7 +661,9 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
     }
     if ((r.flags & (kRecFirst | kRecOpen)) == (kRecFirst | kRecOpen))
       hand_off(PieceHandoff{0, 0, r.b, r.h, 0, 0, kHandInstall, 0});
-    if (r.flags & kRecFirst) M::begin_piece(st, p, r.b, r.h);
+    if (r.flags & kRecFirst) {
+      if constexpr (!FUSE) M::begin_piece(st, p, r.b, r.h);  // fused: done above
+    }
     M::compute_tile(st, p, sk, sv, r.ntok, nullptr);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);

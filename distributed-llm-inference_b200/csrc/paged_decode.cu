@@ -168,6 +168,20 @@ FastKernel make_dyn() {
                     2 * (1 + pdb::kTailChunksPerCta)};
 }
 
+template <class M>
+void launch_dyn_fused(const pdb::AttnParams& p, int grid, size_t smem, cudaStream_t st,
+                      const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  launch_pdl(pdb::attn_tma_dyn_kernel<M, true>, dim3(grid), dim3(pdb::DynStreamK<M>::NT), smem,
+             st, p, *kmap, *vmap);
+}
+
+template <class M>
+FastKernel make_dyn_fused() {
+  return FastKernel{reinterpret_cast<const void*>(&pdb::attn_tma_dyn_kernel<M, true>),
+                    &launch_dyn_fused<M>, &pdb::DynStreamK<M>::smem_bytes, M::GP,
+                    pdb::DynStreamK<M>::NT, true, 2 * (1 + pdb::kTailChunksPerCta)};
+}
+
 // cuTensorMapEncodeTiled from the driver (resolved once through the runtime,
 // so the library needs no link-time dependency on libcuda).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -237,6 +251,22 @@ bool pick_simt(int D, int G, FastKernel* out) {
 
 // Tensor-core inner loop, TMA producer warp and dynamic tail (FP16,
 // block_size % 16 == 0). Stage depths keep two CTAs resident per SM.
+bool pick_dyn_fused(int D, int G, FastKernel* out) {
+  if (G > 8) return false;
+  const bool g4 = G <= 4;
+  if (D == 128) {
+    *out = g4 ? make_dyn_fused<pdb::MmaMath<128, 4, 3, pdb::kTma128B>>()
+              : make_dyn_fused<pdb::MmaMath<128, 8, 2, pdb::kTma128B>>();
+    return true;
+  }
+  if (D == 64) {
+    *out = g4 ? make_dyn_fused<pdb::MmaMath<64, 4, 6, pdb::kTma128B>>()
+              : make_dyn_fused<pdb::MmaMath<64, 8, 5, pdb::kTma128B>>();
+    return true;
+  }
+  return false;
+}
+
 bool pick_dyn(int D, int G, FastKernel* out) {
   if (G > 8) return false;
   const bool g4 = G <= 4;
@@ -730,6 +760,69 @@ int pdb_read_device_errors(uint32_t* flags, int clear) {
     if (e != cudaSuccess) return cuda_fail(e, "clear error word");
   }
   *flags = v;
+  return PDB_OK;
+}
+
+int pdb_decode_attention_supported(int64_t batch, int64_t heads, int64_t kv_heads,
+                                   int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                   int dtype) {
+  FastKernel fk;
+  if (dtype != PDB_DTYPE_FLOAT16 || batch <= 0 || kv_heads <= 0 || heads % kv_heads) return 0;
+  const bool tma_ok = block_size % pdb::kUnitTokens == 0 &&
+                      num_blocks * block_size < (int64_t(1) << 31) &&
+                      tensor_map_encoder() != nullptr;
+  return streamk_shape_ok(batch, kv_heads) && tma_ok &&
+         pick_dyn_fused((int)head_dim, (int)(heads / kv_heads), &fk);
+}
+
+int pdb_decode_attention(const void* q, const void* k_new, const void* v_new, void* k_pool,
+                         void* v_pool, const int32_t* tables, const int32_t* lengths,
+                         const float* inv_freq, void* out, int64_t B, int64_t H, int64_t D,
+                         int64_t N, int64_t bs, int64_t KVH, int64_t W, int64_t max_length,
+                         int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_attention_args(B, H, D, N, bs, KVH, D, W, max_length, dtype);
+  if (rc) return rc;
+  if (!q || !k_new || !v_new || !k_pool || !v_pool || !tables || !lengths || !inv_freq || !out)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!pdb_decode_attention_supported(B, H, KVH, D, N, bs, dtype) || !aligned16(q) ||
+      !aligned16(k_pool) || !aligned16(v_pool))
+    return fail(PDB_ERR_INVALID_ARGUMENT,
+                "fused decode attention does not support this shape/alignment");
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(PDB_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  int dev = 0;
+  if ((rc = current_device(&dev))) return rc;
+  FastKernel fk;
+  pick_dyn_fused((int)D, (int)(H / KVH), &fk);
+  const int64_t grid = fast_grid(dev, fk, B, KVH, max_length);
+  if (grid <= 0) return fail(PDB_ERR_CUDA, "fast kernel cannot be resident on this device");
+  const FastWs ws = fast_ws_layout(B, KVH, D, fk, grid);
+  if (!workspace || workspace_bytes < ws.total)
+    return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) +
+                                       " bytes");
+  pdb::AttnParams p{};
+  p.q = q; p.k_pool = k_pool; p.v_pool = v_pool;
+  p.tables = tables; p.lengths = lengths; p.out = out;
+  p.B = (int)B; p.H = (int)H; p.KVH = (int)KVH; p.G = (int)(H / KVH); p.D = (int)D;
+  p.num_blocks = N; p.block_size = (int)bs;
+  p.bs_shift = ((bs & (bs - 1)) == 0) ? __builtin_ctzll((unsigned long long)bs) : -1;
+  p.table_width = (int)W;
+  p.max_length = (int)max_length;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
+  unsigned char* wb = static_cast<unsigned char*>(workspace);
+  p.counters = reinterpret_cast<unsigned long long*>(wb + ws.counters_off);
+  p.partials = reinterpret_cast<float*>(wb + ws.partials_off);
+  p.call_tag = next_call_tag();
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.inv_freq = inv_freq;
+  CUtensorMap kmap, vmap;
+  if (!(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
+        encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
+    return fail(PDB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV pools");
+  fk.launch(p, (int)grid, fk.smem((int)B), static_cast<cudaStream_t>(stream), &kmap, &vmap);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
   return PDB_OK;
 }
 

@@ -6,9 +6,11 @@ modules (norms, projections, MLP), this class runs prefill and decode with
 the cache access on this library's kernels:
 
 * decode (worker/llama.py:151-177): the batch's tables and lengths live on
-  the GPU (``DevicePagedKV``); per layer one ``rope_kv_write_decode`` (RoPE of
-  q and k, k/v written to the new token's slot, the step's lengths advanced by
-  the first layer) and one ``paged_attention``. A step needs no host-side
+  the GPU (``DevicePagedKV``); per layer one ``decode_attention`` launch (RoPE
+  of q and k, k/v written to the new token's slot, attention) after the
+  step's lengths are advanced once on the device — or, for shapes the fused
+  kernel does not cover, ``rope_kv_write_decode`` (the first layer advancing
+  the lengths) followed by ``paged_attention``. A step needs no host-side
   slot, position or metadata tensors, so with ``graphs=True`` the whole tick
   (embedding, every layer, final norm, LM head) is captured once per batch
   size as a CUDA graph and replayed; only the new token ids are copied in.
@@ -26,7 +28,8 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from .ops import paged_attention, prefill_attention, rope_kv_write, rope_kv_write_decode
+from .ops import (decode_attention, decode_attention_supported, paged_attention,
+                  prefill_attention, rope_kv_write, rope_kv_write_decode)
 from .paged_kv import DevicePagedKV
 
 
@@ -84,6 +87,11 @@ def _tick(runner, cache, token_tensor, tables, lengths, max_length):
     """Embedding -> layers -> norm -> LM head for one decode token per sequence."""
     batch = token_tensor.size(0)
     x = runner.model.model.embed_tokens(token_tensor)
+    fused = decode_attention_supported(
+        torch.empty((batch, runner.heads, runner.head_dim), dtype=runner.dtype,
+                    device="meta"), cache.keys[0]) if runner.dtype == torch.float16 else False
+    if fused:
+        lengths.add_(1)  # the new token (PagedLlama.decode, worker/llama.py:157-158)
     for index, layer in enumerate(runner.model.model.layers):
         residual = x
         normalized = layer.input_layernorm(x)
@@ -91,11 +99,15 @@ def _tick(runner, cache, token_tensor, tables, lengths, max_length):
         q = attn.q_proj(normalized).view(batch, runner.heads, runner.head_dim)
         k = attn.k_proj(normalized).view(batch, runner.kv_heads, runner.head_dim)
         v = attn.v_proj(normalized).view(batch, runner.kv_heads, runner.head_dim)
-        q, k = rope_kv_write_decode(q, k, v, cache.keys[index], cache.values[index], tables,
-                                    lengths, runner.inv_freq, advance=index == 0,
-                                    inplace=True)
-        context = paged_attention(q, cache.keys[index], cache.values[index], tables, lengths,
-                                  max_length)
+        if fused:
+            context = decode_attention(q, k, v, cache.keys[index], cache.values[index], tables,
+                                       lengths, runner.inv_freq, max_length)
+        else:
+            q, k = rope_kv_write_decode(q, k, v, cache.keys[index], cache.values[index],
+                                        tables, lengths, runner.inv_freq,
+                                        advance=index == 0, inplace=True)
+            context = paged_attention(q, cache.keys[index], cache.values[index], tables,
+                                      lengths, max_length)
         x = residual + attn.o_proj(context.reshape(batch, 1, -1))
         x = x + layer.mlp(layer.post_attention_layernorm(x))
     return runner.model.lm_head(runner.model.model.norm(x[:, 0])).float()

@@ -263,6 +263,61 @@ def rope_kv_write_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return q_out, k_out
 
 
+def decode_attention_supported(q: torch.Tensor, k_pool: torch.Tensor) -> bool:
+    """Whether ``decode_attention`` covers this shape (FP16, head_dim 64/128,
+    group <= 8, block_size a multiple of 16) on the current device."""
+    if q.dim() != 3 or k_pool.dim() != 4 or q.dtype != torch.float16:
+        return False
+    B, H, D = q.shape  # q may be a meta tensor: only its shape and dtype are read
+    N, bs, KVH, _ = k_pool.shape
+    with _DeviceGuard(k_pool.device):
+        return bool(_lib.load().pdb_decode_attention_supported(B, H, KVH, D, N, bs,
+                                                               _DTYPES[q.dtype]))
+
+
+def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor,
+                     v_pool: torch.Tensor, tables: torch.Tensor, lengths: torch.Tensor,
+                     inv_freq: torch.Tensor, max_length: int, *,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode layer in one launch (worker/llama.py:168-174).
+
+    ``rope_kv_write_decode(..., advance=False)`` followed by
+    ``paged_attention``, fused: q [B, H, D] and the new token's k, v
+    [B, KVH, D] un-rotated (none of them is modified), lengths already
+    counting the new token (its position is lengths[b] - 1). The rotated k
+    and v are written to the token's slot; returns the attention output
+    [B, H, D], bit-identical to the two-launch path. FP16 only (see
+    ``decode_attention_supported``).
+    """
+    _check_attention_inputs(q, k_pool, v_pool, tables, lengths, max_length)
+    B, H, D = q.shape
+    N, bs, KVH, _ = k_pool.shape
+    for t in (k, v):
+        _check(t.shape == (B, KVH, D) and t.dtype == q.dtype and t.device == q.device
+               and t.is_contiguous(), "invalid new k/v")
+    _check(inv_freq.dtype == torch.float32 and inv_freq.numel() == D // 2
+           and inv_freq.device == q.device and inv_freq.is_contiguous(), "invalid inv_freq")
+    if out is None:
+        out = torch.empty_like(q)
+    else:
+        _check(out.shape == q.shape and out.dtype == q.dtype and out.is_contiguous()
+               and out.device == q.device, "invalid output tensor")
+    lib = _lib.load()
+    dt = _DTYPES[q.dtype]
+    with _DeviceGuard(q.device):
+        stream = _stream_ptr(q.device)
+        need = lib.pdb_paged_attention_workspace_size(B, H, KVH, D, int(max_length), dt)
+        ws = workspace(q.device, stream, need, "attention")
+        rc = lib.pdb_decode_attention(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+            tables.data_ptr(), lengths.data_ptr(), inv_freq.data_ptr(), out.data_ptr(), B, H, D,
+            N, bs, KVH, tables.size(1), int(max_length), dt,
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            stream)
+    _lib.check(rc, "decode_attention")
+    return out
+
+
 def prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                       tables: torch.Tensor, lengths: torch.Tensor, *,
                       out: torch.Tensor | None = None) -> torch.Tensor:

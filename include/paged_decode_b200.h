@@ -239,6 +239,39 @@ PDB_API int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch,
                             int64_t kv_heads, int64_t grid, int64_t* ranges);
 
 /*
+ * One decode layer in one launch: the RoPE + KV-slot write of
+ * pdb_rope_kv_write_decode (advance = 0) and the attention of
+ * pdb_paged_attention, fused into the FP16 stream-K kernel.
+ * Replaces: worker/llama.py:168-174 (rope, the two slot writes, attention)
+ * for a decode step, given lengths that already count the new token.
+ *   q            FP16 [B, H, D], NOT rotated (the kernel rotates it at
+ *                position lengths[b] - 1; q itself is not modified)
+ *   k_new, v_new FP16 [B, KVH, D], the new token's k (not rotated) and v
+ *   k_pool, v_pool, tables, lengths, max_length, out, workspace: as for
+ *                pdb_paged_attention; the new token's rotated k and its v
+ *                are written to slot (tables[b][pos / bs], pos % bs),
+ *                pos = lengths[b] - 1, exactly as pdb_rope_kv_write_decode
+ *                writes them
+ *   inv_freq     fp32 [D/2]
+ * Results are bit-identical to pdb_rope_kv_write_decode followed by
+ * pdb_paged_attention. Shapes the fused kernel does not cover return
+ * PDB_ERR_INVALID_ARGUMENT (see pdb_decode_attention_supported); use the
+ * two calls for them.
+ */
+PDB_API int pdb_decode_attention(const void* q, const void* k_new, const void* v_new,
+                                 void* k_pool, void* v_pool, const int32_t* tables,
+                                 const int32_t* lengths, const float* inv_freq, void* out,
+                                 int64_t batch, int64_t heads, int64_t head_dim,
+                                 int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                                 int64_t table_width, int64_t max_length, int dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* 1 when pdb_decode_attention covers this shape on the current device, else 0. */
+PDB_API int pdb_decode_attention_supported(int64_t batch, int64_t heads, int64_t kv_heads,
+                                           int64_t head_dim, int64_t num_blocks,
+                                           int64_t block_size, int dtype);
+
+/*
  * Causal attention of a prefill batch, K/V read from the paged pools.
  * Replaces: the prefill attention of worker/llama.py:141-144,
  *   SDPA(q^T, repeat_interleave(k)^T, repeat_interleave(v)^T, is_causal=True)

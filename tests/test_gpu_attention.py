@@ -256,3 +256,33 @@ def test_random_shapes(pkg, cuda, seed):
 
 def test_no_device_errors_raised(pkg, cuda):
     assert pkg.read_device_errors() == 0
+
+
+@pytest.mark.parametrize("shape", ["llama3", "smollm"])
+def test_fused_decode_layer_equals_two_launches(pkg, cuda, shape):
+    """decode_attention (RoPE + slot writes folded into the attention kernel)
+    is bit-identical to rope_kv_write_decode + paged_attention: same output,
+    same pool bytes everywhere."""
+    g = torch.Generator().manual_seed(17)
+    if shape == "llama3":
+        w = W.llama3_8b(batch=96, layers=1)
+        B, H, KVH, D = 96, 32, 8, 128
+    else:
+        w = W.smollm_fp16(batch=64, layers=1)
+        B, H, KVH, D = 64, 9, 3, 64
+    t = W.materialize(w, cuda)
+    q = torch.randn(B, H, D, generator=g).half().to(cuda)
+    k = torch.randn(B, KVH, D, generator=g).half().to(cuda)
+    v = torch.randn(B, KVH, D, generator=g).half().to(cuda)
+    assert pkg.decode_attention_supported(q, t.k_pools[0])
+    kp1, vp1 = t.k_pools[0].clone(), t.v_pools[0].clone()
+    kp2, vp2 = t.k_pools[0].clone(), t.v_pools[0].clone()
+    fused = pkg.decode_attention(q, k, v, kp1, vp1, t.tables, t.lengths, t.inv_freq,
+                                 w.max_length)
+    qr, _ = pkg.rope_kv_write_decode(q, k, v, kp2, vp2, t.tables, t.lengths, t.inv_freq)
+    two = pkg.paged_attention(qr, kp2, vp2, t.tables, t.lengths, w.max_length)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, two)
+    assert torch.equal(kp1, kp2) and torch.equal(vp1, vp2)
+    assert not torch.equal(kp1, t.k_pools[0])  # the new tokens were written
+    assert pkg.read_device_errors() == 0
