@@ -426,8 +426,8 @@ def run_ours(args):
     ms_attn = time_graph(g_attn, reps, stream) / (reps * w.layers)
     ms_pro = time_graph(g_pro, reps, stream) / (reps * w.layers) if g_pro is not None else None
     ms_two = time_graph(g_two, reps, stream) / reps if g_two is not None else None
-    # the fused launch does the prologue's work too, so it is charged its bytes
-    attn_bytes = w.attention_bytes() + (w.prologue_bytes() if step.fused else 0)
+    # the fused launch also reads the new k/v and writes their slots
+    attn_bytes = w.fused_bytes() if step.fused else w.attention_bytes()
     peaks = {}
     pk = REPO / "MEASURED_PEAKS.json"
     if pk.exists():

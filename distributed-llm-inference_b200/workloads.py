@@ -97,6 +97,15 @@ class DecodeWorkload:
         writes = (self.heads + 3 * self.kv_heads) * self.head_dim * e
         return self.batch * (per_row + writes + 3 * 8) + 4 * (self.head_dim // 2)
 
+    def fused_bytes(self) -> int:
+        """Algorithmic bytes of one decode_attention launch (RoPE + slot write +
+        attention of one layer): the attention bytes, plus each sequence's new
+        k and v read and written to its slot, plus inv_freq. The fused launch
+        writes no rotated q or k outputs."""
+        e = self.elem_bytes
+        return (self.attention_bytes() + 4 * self.batch * self.kv_heads * self.head_dim * e
+                + 4 * (self.head_dim // 2))
+
     def seq_step_bytes(self) -> int:
         """Per decode step, all layers: prologue + attention bytes."""
         return self.layers * (self.attention_bytes() + self.prologue_bytes())
