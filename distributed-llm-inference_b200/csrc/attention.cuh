@@ -358,13 +358,18 @@ __device__ __forceinline__ void load_tile(const AttnParams& p, const int* Ls, co
 //                (chunk XOR (row & 7)); written by cp.async.bulk.tensor.
 enum : int { kRowSwizzle = 0, kTma128B = 1 };
 
-template <int D_, int GQ_, int STAGES_, int LAYOUT_ = kRowSwizzle>
+// SUB: 16-token blocks per warp per tile (TILE = 64 * SUB tokens). Two
+// blocks per warp give the QK chains of one tile twice the independent work
+// and share one max reduction and one rescale per tile, which pays where a
+// 64-token tile carries few bytes (head_dim 64).
+template <int D_, int GQ_, int STAGES_, int LAYOUT_ = kRowSwizzle, int SUB_ = 1>
 struct MmaMath {
   using T = __half;
-  static constexpr int D = D_, GP = GQ_, STAGES = STAGES_, LAYOUT = LAYOUT_;
+  static constexpr int D = D_, GP = GQ_, STAGES = STAGES_, LAYOUT = LAYOUT_, SUB = SUB_;
+  static_assert(SUB_ == 1 || LAYOUT_ == kTma128B, "multi-block tiles are staged by TMA");
   static constexpr int NW = 4, NT = 128;
-  static constexpr int WT = 16;          // tokens per warp per tile (MMA M)
-  static constexpr int TILE = NW * WT;   // 64 tokens
+  static constexpr int WT = 16 * SUB;    // tokens per warp per tile (SUB x MMA M)
+  static constexpr int TILE = NW * WT;   // 64 * SUB tokens
   static constexpr int TILE_UNITS = TILE / kUnitTokens;
   static constexpr bool SWZ = true;
   static constexpr int KSTEPS = D / 16;  // QK k-steps == PV m-tiles
@@ -415,25 +420,34 @@ struct MmaMath {
     if (r0 >= ntok) return;  // warp-uniform: no valid token in this warp's rows
     const int g = lane >> 2, mi = lane >> 3;
 
-    // S^T[16 tokens x 8 heads] = K[16 x D] . Q^T[D x 8]; two chains for ILP
-    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-      const int row = r0 + ((mi & 1) << 3) + (lane & 7);
+    // S^T[16 tokens x 8 heads] = K[16 x D] . Q^T[D x 8] per 16-token block;
+    // two chains per block for ILP
+    const float sc = p.scale_log2;
+    float sA[SUB][2], sB[SUB][2];  // [block][token g, g+8]: heads 2tg, 2tg+1
+#pragma unroll
+    for (int sb = 0; sb < SUB; ++sb) {
+      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+      const int row = r0 + 16 * sb + ((mi & 1) << 3) + (lane & 7);
 #pragma unroll
       for (int ks = 0; ks < KSTEPS; ++ks) {
         uint32_t a0, a1, a2, a3;
         ldsm_x4(a0, a1, a2, a3, sk + offset(row, 2 * ks + (mi >> 1)));
         mma_16816((ks & 1) ? c1 : c0, a0, a1, a2, a3, s.qb[ks][0], s.qb[ks][1]);
       }
+      const int t = r0 + 16 * sb + g;
+      const bool v0 = t < ntok, v1 = t + 8 < ntok;
+      sA[sb][0] = v0 ? (c0[0] + c1[0]) * sc : -INFINITY;  // token g,   head 2tg
+      sB[sb][0] = v0 ? (c0[1] + c1[1]) * sc : -INFINITY;  // token g,   head 2tg+1
+      sA[sb][1] = v1 ? (c0[2] + c1[2]) * sc : -INFINITY;  // token g+8, head 2tg
+      sB[sb][1] = v1 ? (c0[3] + c1[3]) * sc : -INFINITY;  // token g+8, head 2tg+1
     }
-    const bool v0 = r0 + g < ntok, v1 = r0 + g + 8 < ntok;
-    const float sc = p.scale_log2;
-    const float sA0 = v0 ? (c0[0] + c1[0]) * sc : -INFINITY;  // token g,   head 2tg
-    const float sB0 = v0 ? (c0[1] + c1[1]) * sc : -INFINITY;  // token g,   head 2tg+1
-    const float sA1 = v1 ? (c0[2] + c1[2]) * sc : -INFINITY;  // token g+8, head 2tg
-    const float sB1 = v1 ? (c0[3] + c1[3]) * sc : -INFINITY;  // token g+8, head 2tg+1
 
-    float mA = fmaxf(sA0, sA1), mB = fmaxf(sB0, sB1);
+    float mA = -INFINITY, mB = -INFINITY;
+#pragma unroll
+    for (int sb = 0; sb < SUB; ++sb) {
+      mA = fmaxf(mA, fmaxf(sA[sb][0], sA[sb][1]));
+      mB = fmaxf(mB, fmaxf(sB[sb][0], sB[sb][1]));
+    }
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       mA = fmaxf(mA, __shfl_xor_sync(0xffffffffu, mA, o));
@@ -454,29 +468,38 @@ struct MmaMath {
       s.m[0] = nA;
       s.m[1] = nB;
     }
-    const float pA0 = (sA0 == -INFINITY) ? 0.f : exp2f(sA0 - s.m[0]);
-    const float pB0 = (sB0 == -INFINITY) ? 0.f : exp2f(sB0 - s.m[1]);
-    const float pA1 = (sA1 == -INFINITY) ? 0.f : exp2f(sA1 - s.m[0]);
-    const float pB1 = (sB1 == -INFINITY) ? 0.f : exp2f(sB1 - s.m[1]);
-    s.l[0] += pA0 + pA1;
-    s.l[1] += pB0 + pB1;
+    uint32_t bh0[SUB], bh1[SUB], bl0[SUB], bl1[SUB];
+#pragma unroll
+    for (int sb = 0; sb < SUB; ++sb) {
+      const float pA0 = (sA[sb][0] == -INFINITY) ? 0.f : exp2f(sA[sb][0] - s.m[0]);
+      const float pB0 = (sB[sb][0] == -INFINITY) ? 0.f : exp2f(sB[sb][0] - s.m[1]);
+      const float pA1 = (sA[sb][1] == -INFINITY) ? 0.f : exp2f(sA[sb][1] - s.m[0]);
+      const float pB1 = (sB[sb][1] == -INFINITY) ? 0.f : exp2f(sB[sb][1] - s.m[1]);
+      s.l[0] += pA0 + pA1;
+      s.l[1] += pB0 + pB1;
+      // P^T as two FP16 B operands (hi + lo): the transposes of the C fragment.
+      const uint32_t h0 = pack_half2(pA0, pB0), h1 = pack_half2(pA1, pB1);
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&h1));
+      const uint32_t l0 = pack_half2(pA0 - f0.x, pB0 - f0.y),
+                     l1 = pack_half2(pA1 - f1.x, pB1 - f1.y);
+      bh0[sb] = movmatrix_t(h0);
+      bh1[sb] = movmatrix_t(h1);
+      bl0[sb] = movmatrix_t(l0);
+      bl1[sb] = movmatrix_t(l1);
+    }
 
-    // P^T as two FP16 B operands (hi + lo): the transposes of the C fragment.
-    const uint32_t h0 = pack_half2(pA0, pB0), h1 = pack_half2(pA1, pB1);
-    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
-    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&h1));
-    const uint32_t l0 = pack_half2(pA0 - f0.x, pB0 - f0.y), l1 = pack_half2(pA1 - f1.x, pB1 - f1.y);
-    const uint32_t bh0 = movmatrix_t(h0), bh1 = movmatrix_t(h1);
-    const uint32_t bl0 = movmatrix_t(l0), bl1 = movmatrix_t(l1);
-
-    // O^T[D x 8] += V^T[D x 16 tokens] . P^T[16 x 8]
+    // O^T[D x 8] += V^T[D x 16 tokens] . P^T[16 x 8], block by block
     const int vrow = r0 + ((mi >> 1) << 3) + (lane & 7);
 #pragma unroll
     for (int md = 0; md < KSTEPS; ++md) {
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4_t(a0, a1, a2, a3, sv + offset(vrow, 2 * md + (mi & 1)));
-      mma_16816(s.acc[md], a0, a1, a2, a3, bh0, bh1);
-      mma_16816(s.acc[md], a0, a1, a2, a3, bl0, bl1);
+#pragma unroll
+      for (int sb = 0; sb < SUB; ++sb) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(a0, a1, a2, a3, sv + offset(vrow + 16 * sb, 2 * md + (mi & 1)));
+        mma_16816(s.acc[md], a0, a1, a2, a3, bh0[sb], bh1[sb]);
+        mma_16816(s.acc[md], a0, a1, a2, a3, bl0[sb], bl1[sb]);
+      }
     }
   }
 

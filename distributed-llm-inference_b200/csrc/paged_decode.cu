@@ -260,8 +260,8 @@ bool pick_dyn_fused(int D, int G, FastKernel* out) {
     return true;
   }
   if (D == 64) {
-    *out = g4 ? make_dyn_fused<pdb::MmaMath<64, 4, 6, pdb::kTma128B>>()
-              : make_dyn_fused<pdb::MmaMath<64, 8, 5, pdb::kTma128B>>();
+    *out = g4 ? make_dyn_fused<pdb::MmaMath<64, 4, 3, pdb::kTma128B, 2>>()
+              : make_dyn_fused<pdb::MmaMath<64, 8, 3, pdb::kTma128B, 2>>();
     return true;
   }
   return false;
@@ -276,8 +276,8 @@ bool pick_dyn(int D, int G, FastKernel* out) {
     return true;
   }
   if (D == 64) {
-    *out = g4 ? make_dyn<pdb::MmaMath<64, 4, 6, pdb::kTma128B>>()
-              : make_dyn<pdb::MmaMath<64, 8, 5, pdb::kTma128B>>();
+    *out = g4 ? make_dyn<pdb::MmaMath<64, 4, 3, pdb::kTma128B, 2>>()
+              : make_dyn<pdb::MmaMath<64, 8, 3, pdb::kTma128B, 2>>();
     return true;
   }
   return false;
