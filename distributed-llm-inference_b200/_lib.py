@@ -38,7 +38,8 @@ SIGNATURES = {
     "pdb_rope_kv_write_workspace_size": (_c_size, [_c_i64, _c_i64, _c_int]),
     "pdb_decode_attention": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
                                       _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
-                                      _c_i64, _c_i64, _c_i64, _c_int, _c_ptr, _c_size, _c_ptr]),
+                                      _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_ptr,
+                                      _c_size, _c_ptr]),
     "pdb_decode_attention_supported": (_c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                                 _c_int]),
     "pdb_prefill_attention": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64,

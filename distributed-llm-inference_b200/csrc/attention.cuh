@@ -69,6 +69,8 @@ struct AttnParams {
   const void* k_new;
   const void* v_new;
   const float* inv_freq;
+  int64_t q_row;   // fused: elements between consecutive sequences' q rows (H * D if packed)
+  int64_t kv_row;  // fused: same for k_new / v_new (KVH * D if packed)
 };
 
 // Clamp a length read from device memory into [0, max_length].

@@ -278,8 +278,8 @@ __device__ __forceinline__ void fused_piece_start(typename M::State& st, const A
   static_assert(KS % 2 == 0, "lower and upper halves in whole k-steps");
   const int tid = threadIdx.x, lane = tid & 31, g = lane >> 2, tg = lane & 3;
   const bool real = g < p.G;  // columns >= G are padding (q = 0)
-  const __half* qrow = static_cast<const __half*>(p.q) +
-                       ((int64_t)b * p.H + (int64_t)h * p.G + (real ? g : 0)) * D;
+  const __half* qrow = static_cast<const __half*>(p.q) + (int64_t)b * p.q_row +
+                       ((int64_t)h * p.G + (real ? g : 0)) * D;
   __half2 qx1[KS / 2][2], qx2[KS / 2][2];
 #pragma unroll
   for (int ks = 0; ks < KS / 2; ++ks)
@@ -290,7 +290,7 @@ __device__ __forceinline__ void fused_piece_start(typename M::State& st, const A
       qx2[ks][r] = *reinterpret_cast<const __half2*>(qrow + i + HALF);
     }
   __half k1 = __float2half_rn(0.f), k2 = k1, v1 = k1, v2 = k1;
-  const int64_t src = ((int64_t)b * p.KVH + h) * D;
+  const int64_t src = (int64_t)b * p.kv_row + (int64_t)h * D;
   if (new_tok && tid < HALF) {
     k1 = static_cast<const __half*>(p.k_new)[src + tid];
     k2 = static_cast<const __half*>(p.k_new)[src + tid + HALF];

@@ -779,15 +779,20 @@ int pdb_decode_attention(const void* q, const void* k_new, const void* v_new, vo
                          void* v_pool, const int32_t* tables, const int32_t* lengths,
                          const float* inv_freq, void* out, int64_t B, int64_t H, int64_t D,
                          int64_t N, int64_t bs, int64_t KVH, int64_t W, int64_t max_length,
-                         int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+                         int64_t q_row_stride, int64_t kv_row_stride, int dtype,
+                         void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_attention_args(B, H, D, N, bs, KVH, D, W, max_length, dtype);
   if (rc) return rc;
   if (!q || !k_new || !v_new || !k_pool || !v_pool || !tables || !lengths || !inv_freq || !out)
     return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  if (!pdb_decode_attention_supported(B, H, KVH, D, N, bs, dtype) || !aligned16(q) ||
-      !aligned16(k_pool) || !aligned16(v_pool))
+  if (!pdb_decode_attention_supported(B, H, KVH, D, N, bs, dtype) || !aligned16(k_pool) ||
+      !aligned16(v_pool) || (reinterpret_cast<uintptr_t>(q) & 3u))
     return fail(PDB_ERR_INVALID_ARGUMENT,
                 "fused decode attention does not support this shape/alignment");
+  const int64_t q_row = q_row_stride ? q_row_stride : H * D;
+  const int64_t kv_row = kv_row_stride ? kv_row_stride : KVH * D;
+  if (q_row < H * D || kv_row < KVH * D || (q_row & 1))
+    return fail(PDB_ERR_INVALID_ARGUMENT, "invalid row strides");
   if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return fail(PDB_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   int dev = 0;
@@ -816,6 +821,8 @@ int pdb_decode_attention(const void* q, const void* k_new, const void* v_new, vo
   p.k_new = k_new;
   p.v_new = v_new;
   p.inv_freq = inv_freq;
+  p.q_row = q_row;
+  p.kv_row = kv_row;
   CUtensorMap kmap, vmap;
   if (!(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
         encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))

@@ -83,6 +83,42 @@ class _TickGraph:
         return self.logits
 
 
+def _fused_weights(layer):
+    """The layer's q/k/v and gate/up projections as one weight each, so a
+    decode tick runs one GEMM for q, k, v and one for gate, up. The modules'
+    weights become views of them: the same values, no extra memory. Layers
+    with projection biases keep their modules (returns None)."""
+    cached = layer.__dict__.get("_b200_fused")
+    if cached is not None:
+        return cached or None
+    attn, mlp = layer.self_attn, layer.mlp
+    mods = (attn.q_proj, attn.k_proj, attn.v_proj, attn.o_proj, mlp.gate_proj, mlp.up_proj,
+            mlp.down_proj)
+    if any(getattr(m, "bias", None) is not None for m in mods):
+        layer._b200_fused = False
+        return None
+
+    def fuse(group):
+        w = torch.cat([m.weight.detach() for m in group], 0)
+        off = 0
+        for m in group:
+            n = m.weight.shape[0]
+            m.weight = torch.nn.Parameter(w[off:off + n], requires_grad=False)
+            off += n
+        return w
+
+    with torch.no_grad():
+        layer._b200_fused = (fuse((attn.q_proj, attn.k_proj, attn.v_proj)),
+                             fuse((mlp.gate_proj, mlp.up_proj)))
+    return layer._b200_fused
+
+
+def _rms_norm(norm, x):
+    """LlamaRMSNorm in one fused op (fp32 statistics, one rounding)."""
+    eps = getattr(norm, "variance_epsilon", None) or getattr(norm, "eps", 1e-6)
+    return F.rms_norm(x, (x.shape[-1],), norm.weight, eps)
+
+
 def _tick(runner, cache, token_tensor, tables, lengths, max_length):
     """Embedding -> layers -> norm -> LM head for one decode token per sequence."""
     batch = token_tensor.size(0)
@@ -92,7 +128,27 @@ def _tick(runner, cache, token_tensor, tables, lengths, max_length):
                     device="meta"), cache.keys[0]) if runner.dtype == torch.float16 else False
     if fused:
         lengths.add_(1)  # the new token (PagedLlama.decode, worker/llama.py:157-158)
+    H, KVH, D = runner.heads, runner.kv_heads, runner.head_dim
     for index, layer in enumerate(runner.model.model.layers):
+        weights = _fused_weights(layer) if fused else None
+        if weights is not None:
+            # one GEMM for q/k/v (the attention reads its row slices), the
+            # residual adds folded into the o and down GEMMs (addmm)
+            wqkv, wgu = weights
+            attn, mlp = layer.self_attn, layer.mlp
+            x2 = x.view(batch, -1)
+            qkv = F.linear(_rms_norm(layer.input_layernorm, x2), wqkv)
+            q = qkv[:, :H * D].view(batch, H, D)
+            k = qkv[:, H * D:(H + KVH) * D].view(batch, KVH, D)
+            v = qkv[:, (H + KVH) * D:].view(batch, KVH, D)
+            context = decode_attention(q, k, v, cache.keys[index], cache.values[index], tables,
+                                       lengths, runner.inv_freq, max_length)
+            x2 = torch.addmm(x2, context.view(batch, -1), attn.o_proj.weight.t())
+            gu = F.linear(_rms_norm(layer.post_attention_layernorm, x2), wgu)
+            inter = wgu.shape[0] // 2
+            act = mlp.act_fn(gu[:, :inter]) * gu[:, inter:]
+            x = torch.addmm(x2, act, mlp.down_proj.weight.t()).view(batch, 1, -1)
+            continue
         residual = x
         normalized = layer.input_layernorm(x)
         attn = layer.self_attn

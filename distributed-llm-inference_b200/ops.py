@@ -283,18 +283,26 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
 
     ``rope_kv_write_decode(..., advance=False)`` followed by
     ``paged_attention``, fused: q [B, H, D] and the new token's k, v
-    [B, KVH, D] un-rotated (none of them is modified), lengths already
+    [B, KVH, D] un-rotated (none of them is modified; each may be a row
+    slice of one fused q/k/v projection output), lengths already
     counting the new token (its position is lengths[b] - 1). The rotated k
     and v are written to the token's slot; returns the attention output
     [B, H, D], bit-identical to the two-launch path. FP16 only (see
     ``decode_attention_supported``).
     """
-    _check_attention_inputs(q, k_pool, v_pool, tables, lengths, max_length)
+    # q, k and v may be row slices of one fused projection output: heads packed
+    # within a sequence (strides (row, D, 1)), any row stride between sequences
+    _check(q.is_cuda and q.dim() == 3 and q.stride(2) == 1 and q.stride(1) == q.size(2)
+           and q.stride(0) >= q.size(1) * q.size(2), "query heads must be packed in each row")
+    qc = q if q.is_contiguous() else q.as_strided(q.shape, (q.size(1) * q.size(2), q.size(2), 1))
+    _check_attention_inputs(qc, k_pool, v_pool, tables, lengths, max_length)
     B, H, D = q.shape
     N, bs, KVH, _ = k_pool.shape
     for t in (k, v):
         _check(t.shape == (B, KVH, D) and t.dtype == q.dtype and t.device == q.device
-               and t.is_contiguous(), "invalid new k/v")
+               and t.stride(2) == 1 and t.stride(1) == D and t.stride(0) >= KVH * D,
+               "invalid new k/v")
+    _check(k.stride(0) == v.stride(0), "k and v rows must have the same stride")
     _check(inv_freq.dtype == torch.float32 and inv_freq.numel() == D // 2
            and inv_freq.device == q.device and inv_freq.is_contiguous(), "invalid inv_freq")
     if out is None:
@@ -311,7 +319,7 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
         rc = lib.pdb_decode_attention(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
             tables.data_ptr(), lengths.data_ptr(), inv_freq.data_ptr(), out.data_ptr(), B, H, D,
-            N, bs, KVH, tables.size(1), int(max_length), dt,
+            N, bs, KVH, tables.size(1), int(max_length), q.stride(0), k.stride(0), dt,
             ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
             stream)
     _lib.check(rc, "decode_attention")

@@ -245,8 +245,11 @@ PDB_API int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch,
  * Replaces: worker/llama.py:168-174 (rope, the two slot writes, attention)
  * for a decode step, given lengths that already count the new token.
  *   q            FP16 [B, H, D], NOT rotated (the kernel rotates it at
- *                position lengths[b] - 1; q itself is not modified)
- *   k_new, v_new FP16 [B, KVH, D], the new token's k (not rotated) and v
+ *                position lengths[b] - 1; q itself is not modified); sequence
+ *                b's heads start at q + b * q_row_stride (elements; 0 = H * D,
+ *                packed), e.g. a slice of a fused q/k/v projection's output
+ *   k_new, v_new FP16 [B, KVH, D], the new token's k (not rotated) and v,
+ *                rows kv_row_stride elements apart (0 = KVH * D)
  *   k_pool, v_pool, tables, lengths, max_length, out, workspace: as for
  *                pdb_paged_attention; the new token's rotated k and its v
  *                are written to slot (tables[b][pos / bs], pos % bs),
@@ -263,7 +266,8 @@ PDB_API int pdb_decode_attention(const void* q, const void* k_new, const void* v
                                  const int32_t* lengths, const float* inv_freq, void* out,
                                  int64_t batch, int64_t heads, int64_t head_dim,
                                  int64_t num_blocks, int64_t block_size, int64_t kv_heads,
-                                 int64_t table_width, int64_t max_length, int dtype,
+                                 int64_t table_width, int64_t max_length,
+                                 int64_t q_row_stride, int64_t kv_row_stride, int dtype,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* 1 when pdb_decode_attention covers this shape on the current device, else 0. */

@@ -286,3 +286,26 @@ def test_fused_decode_layer_equals_two_launches(pkg, cuda, shape):
     assert torch.equal(kp1, kp2) and torch.equal(vp1, vp2)
     assert not torch.equal(kp1, t.k_pools[0])  # the new tokens were written
     assert pkg.read_device_errors() == 0
+
+
+def test_fused_decode_layer_reads_projection_slices(pkg, cuda):
+    """q, k and v given as row slices of one fused q/k/v projection output
+    (row stride (H + 2*KVH) * D) give the same output and pool bytes as
+    contiguous copies."""
+    g = torch.Generator().manual_seed(19)
+    w = W.smollm_fp16(batch=48, layers=1)
+    t = W.materialize(w, cuda)
+    B, H, KVH, D = 48, 9, 3, 64
+    qkv = torch.randn(B, (H + 2 * KVH) * D, generator=g).half().to(cuda)
+    q = qkv[:, :H * D].view(B, H, D)
+    k = qkv[:, H * D:(H + KVH) * D].view(B, KVH, D)
+    v = qkv[:, (H + KVH) * D:].view(B, KVH, D)
+    kp1, vp1 = t.k_pools[0].clone(), t.v_pools[0].clone()
+    kp2, vp2 = t.k_pools[0].clone(), t.v_pools[0].clone()
+    a = pkg.decode_attention(q, k, v, kp1, vp1, t.tables, t.lengths, t.inv_freq, w.max_length)
+    b = pkg.decode_attention(q.contiguous(), k.contiguous(), v.contiguous(), kp2, vp2, t.tables,
+                             t.lengths, t.inv_freq, w.max_length)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert torch.equal(kp1, kp2) and torch.equal(vp1, vp2)
+    assert pkg.read_device_errors() == 0
