@@ -12,9 +12,10 @@
 // One CTA per (64-query tile, query head, prompt); 4 warps, 16 query rows
 // each. Per 64-key tile (double-buffered with cp.async into XOR-swizzled
 // shared memory): S = Q K^T on tensor cores (mma.sync m16n8k16, fp32
-// accumulate), causal and length masks, online softmax in fp32 (base 2), then
-// O += P V with P split into FP16 hi + lo terms (P keeps ~22 bits, as in the
-// decode kernels). Rows at or beyond len_b are written as zeros: with
+// accumulate), causal and length masks (only on the tiles that need them),
+// online softmax in fp32 (base 2), then O += P V with P rounded to FP16 (the
+// precision of the reference's own SDPA kernels). Rows at or beyond len_b are
+// written as zeros: with
 // left-aligned prompts and causal attention no real row attends to them and
 // they feed only padded rows of later layers.
 #pragma once
@@ -164,16 +165,24 @@ __global__ void __launch_bounds__(128) prefill_attention_kernel(const PrefillPar
         mma_16816(s[2 * np + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0b, b1b);
       }
     }
-    // scale, causal and length masks, row maxima
+    // scale; causal and length masks on the diagonal and the last key tile
+    // only (every key of a tile wholly below the diagonal and inside the
+    // prompt is visible to every row); row maxima
+    const bool full = j * 64 + 64 <= t0 && j * 64 + 64 <= kend;
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
+      if (full) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = j * 64 + nt * 8 + 2 * tg + (e & 1);
-        const int qr = e < 2 ? qr0 : qr1;
-        const bool ok = key <= qr && key < kend;
-        s[nt][e] = ok ? s[nt][e] * p.scale_log2 : -INFINITY;
+        for (int e = 0; e < 4; ++e) s[nt][e] *= p.scale_log2;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = j * 64 + nt * 8 + 2 * tg + (e & 1);
+          const int qr = e < 2 ? qr0 : qr1;
+          const bool ok = key <= qr && key < kend;
+          s[nt][e] = ok ? s[nt][e] * p.scale_log2 : -INFINITY;
+        }
       }
       mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
       mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
@@ -197,39 +206,32 @@ __global__ void __launch_bounds__(128) prefill_attention_kernel(const PrefillPar
       o[i][0] *= a0; o[i][1] *= a0;
       o[i][2] *= a1; o[i][3] *= a1;
     }
+    // exp2(-inf - m) = 0 for masked keys (m is finite from the first tile on)
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      s[nt][0] = (s[nt][0] == -INFINITY) ? 0.f : exp2f(s[nt][0] - m0);
-      s[nt][1] = (s[nt][1] == -INFINITY) ? 0.f : exp2f(s[nt][1] - m0);
-      s[nt][2] = (s[nt][2] == -INFINITY) ? 0.f : exp2f(s[nt][2] - m1);
-      s[nt][3] = (s[nt][3] == -INFINITY) ? 0.f : exp2f(s[nt][3] - m1);
+      s[nt][0] = exp2f(s[nt][0] - m0);
+      s[nt][1] = exp2f(s[nt][1] - m0);
+      s[nt][2] = exp2f(s[nt][2] - m1);
+      s[nt][3] = exp2f(s[nt][3] - m1);
       l0 += s[nt][0] + s[nt][1];
       l1 += s[nt][2] + s[nt][3];
     }
-    // O[16 x D] += P[16 x 64] V[64 x D]; P as FP16 hi + lo A operands
+    // O[16 x D] += P[16 x 64] V[64 x D], P as the FP16 A operand:
+    // (row g, keys 0-7), (row g+8, keys 0-7), (g, 8-15), (g+8, 8-15)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      uint32_t ph[4], pl[4];
       const float* c0 = s[2 * kk];
       const float* c1 = s[2 * kk + 1];
-      const float v[8] = {c0[0], c0[1], c0[2], c0[3], c1[0], c1[1], c1[2], c1[3]};
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        ph[r] = pack_half2(v[2 * r], v[2 * r + 1]);
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ph[r]));
-        pl[r] = pack_half2(v[2 * r] - f.x, v[2 * r + 1] - f.y);
-      }
-      // A fragment order: (row g, keys 0-7), (row g+8, keys 0-7), (g, 8-15), (g+8, 8-15)
+      const uint32_t p0 = pack_half2(c0[0], c0[1]), p1 = pack_half2(c0[2], c0[3]);
+      const uint32_t p2 = pack_half2(c1[0], c1[1]), p3 = pack_half2(c1[2], c1[3]);
 #pragma unroll
       for (int dp = 0; dp < DT / 2; ++dp) {
         uint32_t b0x, b1x, b0y, b1y;
         ldsm_x4_t(b0x, b1x, b0y, b1y,
                   sv + tile_offset<ROW, true>(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8,
                                               2 * dp + (lane >> 4)));
-        mma_16816(o[2 * dp], ph[0], ph[1], ph[2], ph[3], b0x, b1x);
-        mma_16816(o[2 * dp], pl[0], pl[1], pl[2], pl[3], b0x, b1x);
-        mma_16816(o[2 * dp + 1], ph[0], ph[1], ph[2], ph[3], b0y, b1y);
-        mma_16816(o[2 * dp + 1], pl[0], pl[1], pl[2], pl[3], b0y, b1y);
+        mma_16816(o[2 * dp], p0, p1, p2, p3, b0x, b1x);
+        mma_16816(o[2 * dp + 1], p0, p1, p2, p3, b0y, b1y);
       }
     }
     __syncthreads();  // the stage is refilled by the next iteration's loads
