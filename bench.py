@@ -70,6 +70,8 @@ def parse():
                     help="how sequences are split over ranks (both give every rank B/P)")
     ap.add_argument("--no-alt", action="store_true",
                     help="at N>1, skip the second measurement with the other sharding")
+    ap.add_argument("--prefill-kernel", choices=["auto", "tcgen05", "mma"], default="auto",
+                    help="pin the prefill attention kernel (prefill workload)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -838,11 +840,15 @@ def run_prefill(args):
         which = "reference prefill attention: repeat_interleave + causal SDPA on the padded batch"
     else:
         out = torch.empty_like(c["q"])
+        impl = {"auto": PKG.PREFILL_AUTO, "tcgen05": PKG.PREFILL_TCGEN05,
+                "mma": PKG.PREFILL_MMA}[args.prefill_kernel]
 
         def step():
             return PKG.prefill_attention(c["q"], c["k_pool"], c["v_pool"], c["tables"],
-                                         c["lengths"], out=out)
-        which = "prefill_attention_kernel<64> (K/V from the paged pools)"
+                                         c["lengths"], out=out, impl=impl)
+        which = ("prefill_attention_kernel<64> (mma.sync; K/V from the paged pools)"
+                 if args.prefill_kernel == "mma" else
+                 "prefill_tc_kernel<64> (tcgen05.mma + TMEM, TMA from the paged pools)")
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):

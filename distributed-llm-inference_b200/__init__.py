@@ -21,6 +21,7 @@ The package directory name contains '-', so import it with
 importlib.import_module("distributed-llm-inference_b200").
 """
 from ._lib import IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA, IMPL_TMA_STATIC, load as load_library  # noqa: F401
+from ._lib import PREFILL_AUTO, PREFILL_MMA, PREFILL_TCGEN05  # noqa: F401
 from .ops import (decode_attention, decode_attention_supported,  # noqa: F401
                   fast_grid_size, paged_attention, prefill_attention, read_device_errors,
                   rope_kv_write, rope_kv_write_decode)
@@ -35,4 +36,5 @@ __all__ = [
     "cuda_paged_attention", "install", "uninstall",
     "read_device_errors", "fast_grid_size", "load_library",
     "IMPL_AUTO", "IMPL_FAST", "IMPL_GENERIC", "IMPL_SIMT", "IMPL_MMA", "IMPL_TMA_STATIC",
+    "PREFILL_AUTO", "PREFILL_TCGEN05", "PREFILL_MMA",
 ]

@@ -45,6 +45,9 @@ SIGNATURES = {
     "pdb_prefill_attention": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64,
                                        _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                        _c_int, _c_ptr]),
+    "pdb_prefill_attention_impl": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                            _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                            _c_i64, _c_i64, _c_int, _c_ptr, _c_int]),
     "pdb_rope_kv_write_decode": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
                                           _c_ptr, _c_i64, _c_ptr, _c_int, _c_ptr, _c_i64,
                                           _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
@@ -58,6 +61,7 @@ SIGNATURES = {
 DTYPE_FLOAT32 = 0
 DTYPE_FLOAT16 = 1
 IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA, IMPL_TMA_STATIC = 0, 1, 2, 3, 4, 5
+PREFILL_AUTO, PREFILL_TCGEN05, PREFILL_MMA = 0, 1, 2
 STATUS_NAMES = {0: "ok", 1: "invalid argument", 2: "workspace", 3: "cuda"}
 
 _lock = threading.Lock()

@@ -22,6 +22,7 @@
 #include "attention_dyn.cuh"
 #include "rope_kv_write.cuh"
 #include "prefill.cuh"
+#include "prefill_tc.cuh"
 
 namespace {
 
@@ -210,6 +211,21 @@ bool encode_pool_map(CUtensorMap* m, const void* pool, int64_t N, int64_t bs, in
   const cuuint32_t box[3] = {64, 1, (cuuint32_t)pdb::kUnitTokens};
   const cuuint32_t estr[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(pool), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Rows [R, heads, D] (FP16, e.g. a padded q batch [B, W, H, D] with R = B*W);
+// box = `rows_box` rows of one head, 64 columns, 128-byte swizzle.
+bool encode_rows_map(CUtensorMap* m, const void* base, int64_t R, int64_t heads, int64_t D,
+                     int rows_box) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)R};
+  const cuuint64_t strides[2] = {(cuuint64_t)(D * 2), (cuuint64_t)(heads * D * 2)};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)rows_box};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -833,11 +849,13 @@ int pdb_decode_attention(const void* q, const void* k_new, const void* v_new, vo
   return PDB_OK;
 }
 
-int pdb_prefill_attention(const void* q, const void* k_pool, const void* v_pool,
-                          const int32_t* tables, const int32_t* lengths, void* out,
-                          int64_t batch, int64_t width, int64_t heads, int64_t head_dim,
-                          int64_t num_blocks, int64_t block_size, int64_t kv_heads,
-                          int64_t table_width, int dtype, void* stream) {
+int pdb_prefill_attention_impl(const void* q, const void* k_pool, const void* v_pool,
+                               const int32_t* tables, const int32_t* lengths, void* out,
+                               int64_t batch, int64_t width, int64_t heads, int64_t head_dim,
+                               int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                               int64_t table_width, int dtype, void* stream, int impl) {
+  if (impl < PDB_PREFILL_AUTO || impl > PDB_PREFILL_MMA)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "unknown prefill kernel");
   if (dtype != PDB_DTYPE_FLOAT16)
     return fail(PDB_ERR_INVALID_ARGUMENT, "prefill attention takes FP16");
   if (!(batch > 0 && width > 0 && heads > 0 && kv_heads > 0))
@@ -853,6 +871,58 @@ int pdb_prefill_attention(const void* q, const void* k_pool, const void* v_pool,
     return fail(PDB_ERR_INVALID_ARGUMENT, "null tensor pointer");
   if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out))
     return fail(PDB_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  // The tensor-core kernel stages whole 16-token units of a page by TMA;
+  // pool rows and q rows are addressed as int32 TMA coordinates.
+  const bool tc_ok = block_size % pdb::kUnitTokens == 0 && num_blocks * block_size <= INT32_MAX &&
+                     batch * width <= INT32_MAX;
+  if (impl == PDB_PREFILL_TCGEN05 && !tc_ok)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "the tcgen05 prefill kernel needs block_size % 16 == 0");
+  const bool use_tc = impl == PDB_PREFILL_TCGEN05 || (impl == PDB_PREFILL_AUTO && tc_ok);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int G = (int)(heads / kv_heads);
+  const int bs_shift = ((block_size & (block_size - 1)) == 0)
+                           ? __builtin_ctzll((unsigned long long)block_size) : -1;
+  const float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+  if (use_tc) {
+    pdb::PrefillTcParams p{};
+    p.tables = tables;
+    p.lengths = lengths;
+    p.out = static_cast<__half*>(out);
+    p.B = (int)batch; p.W = (int)width; p.H = (int)heads; p.KVH = (int)kv_heads; p.G = G;
+    p.table_width = (int)table_width;
+    p.block_size = (int)block_size;
+    p.bs_shift = bs_shift;
+    p.num_blocks = num_blocks;
+    p.scale_log2 = scale_log2;
+    CUtensorMap qmap, kmap, vmap;
+    if (!(encode_rows_map(&qmap, q, batch * width, heads, head_dim, pdb::PrefillTc<64>::BM) &&
+          encode_pool_map(&kmap, k_pool, num_blocks, block_size, kv_heads, head_dim) &&
+          encode_pool_map(&vmap, v_pool, num_blocks, block_size, kv_heads, head_dim)))
+      return fail(PDB_ERR_CUDA, "cuTensorMapEncodeTiled failed for q or the KV pools");
+    const void* fn = head_dim == 64 ? reinterpret_cast<const void*>(&pdb::prefill_tc_kernel<64>)
+                                    : reinterpret_cast<const void*>(&pdb::prefill_tc_kernel<128>);
+    const size_t smem = head_dim == 64 ? pdb::PrefillTc<64>::SMEM : pdb::PrefillTc<128>::SMEM;
+    // Each resident CTA holds 256 TMEM columns: at most two fit an SM's 512.
+    constexpr int NT = pdb::PrefillTc<64>::NT;
+    static_assert(NT == pdb::PrefillTc<128>::NT, "one block size");
+    const int occ = ctas_per_sm(dev, fn, smem, NT);
+    if (occ <= 0 || occ > 2)
+      return fail(PDB_ERR_CUDA, "tcgen05 prefill kernel residency is not 1-2 CTAs per SM");
+    // (query head, prompt, 128-row tile); the kernel maps blockIdx.z to tiles
+    // from the last one down, so the longest tiles are dispatched first.
+    const dim3 grid((unsigned)heads, (unsigned)batch,
+                    (unsigned)((width + pdb::PrefillTc<64>::BM - 1) / pdb::PrefillTc<64>::BM));
+    if (head_dim == 64)
+      e = launch_pdl(pdb::prefill_tc_kernel<64>, grid, dim3(NT), smem, st, p, qmap, kmap, vmap);
+    else
+      e = launch_pdl(pdb::prefill_tc_kernel<128>, grid, dim3(NT), smem, st, p, qmap, kmap, vmap);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "prefill attention launch");
+    return PDB_OK;
+  }
   pdb::PrefillParams p{};
   p.q = static_cast<const __half*>(q);
   p.k_pool = static_cast<const __half*>(k_pool);
@@ -860,24 +930,18 @@ int pdb_prefill_attention(const void* q, const void* k_pool, const void* v_pool,
   p.tables = tables;
   p.lengths = lengths;
   p.out = static_cast<__half*>(out);
-  p.B = (int)batch; p.W = (int)width; p.H = (int)heads; p.KVH = (int)kv_heads;
-  p.G = (int)(heads / kv_heads);
+  p.B = (int)batch; p.W = (int)width; p.H = (int)heads; p.KVH = (int)kv_heads; p.G = G;
   p.table_width = (int)table_width;
   p.block_size = (int)block_size;
-  p.bs_shift = ((block_size & (block_size - 1)) == 0)
-                   ? __builtin_ctzll((unsigned long long)block_size) : -1;
+  p.bs_shift = bs_shift;
   p.num_blocks = num_blocks;
-  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  p.scale_log2 = scale_log2;
   const void* fn = head_dim == 64 ? reinterpret_cast<const void*>(&pdb::prefill_attention_kernel<64>)
                                   : reinterpret_cast<const void*>(&pdb::prefill_attention_kernel<128>);
   const size_t smem = head_dim == 64 ? pdb::PrefillTile<64>::SMEM : pdb::PrefillTile<128>::SMEM;
   if (ctas_per_sm(dev, fn, smem, 128) <= 0)
     return fail(PDB_ERR_CUDA, "prefill attention kernel cannot be resident");
   const dim3 grid((unsigned)((width + 63) / 64), (unsigned)heads, (unsigned)batch);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 64)
     launch_pdl(pdb::prefill_attention_kernel<64>, grid, dim3(128), smem, st, p);
   else
@@ -885,6 +949,16 @@ int pdb_prefill_attention(const void* q, const void* k_pool, const void* v_pool,
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill attention launch");
   return PDB_OK;
+}
+
+int pdb_prefill_attention(const void* q, const void* k_pool, const void* v_pool,
+                          const int32_t* tables, const int32_t* lengths, void* out,
+                          int64_t batch, int64_t width, int64_t heads, int64_t head_dim,
+                          int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                          int64_t table_width, int dtype, void* stream) {
+  return pdb_prefill_attention_impl(q, k_pool, v_pool, tables, lengths, out, batch, width, heads,
+                                    head_dim, num_blocks, block_size, kv_heads, table_width, dtype,
+                                    stream, PDB_PREFILL_AUTO);
 }
 
 int64_t pdb_debug_dyn_partition(int64_t units, int64_t launched, int64_t* ranges,

@@ -328,7 +328,8 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
 
 def prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                       tables: torch.Tensor, lengths: torch.Tensor, *,
-                      out: torch.Tensor | None = None) -> torch.Tensor:
+                      out: torch.Tensor | None = None,
+                      impl: int = _lib.PREFILL_AUTO) -> torch.Tensor:
     """Causal attention of a left-aligned prompt batch, K/V from the paged pools.
 
     The prefill attention of worker/llama.py:141-144 (causal SDPA over the
@@ -336,7 +337,10 @@ def prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tenso
     the repeat: q [B, W, H, D] FP16 (head_dim 64 or 128), pools
     [blocks, bs, KVH, D] holding every prompt token's k/v (as rope_kv_write
     leaves them), tables int32 [B, pages], lengths int32 [B]. Returns
-    [B, W, H, D]; rows at or beyond a prompt's length are zero.
+    [B, W, H, D]; rows at or beyond a prompt's length are zero. `impl` pins
+    the kernel (PREFILL_TCGEN05: tcgen05.mma with TMEM accumulators, needs
+    block_size % 16 == 0; PREFILL_MMA: mma.sync, any block size); the default
+    takes the tcgen05 kernel whenever the block size allows.
     """
     _check(q.is_cuda, "query must be on CUDA")
     for t in (q, k_pool, v_pool, tables, lengths):
@@ -360,10 +364,10 @@ def prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tenso
                and out.device == q.device, "invalid output tensor")
     lib = _lib.load()
     with _DeviceGuard(q.device):
-        rc = lib.pdb_prefill_attention(
+        rc = lib.pdb_prefill_attention_impl(
             q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), tables.data_ptr(),
             lengths.data_ptr(), out.data_ptr(), B, Wd, H, D, N, bs, KVH, tables.size(1),
-            _lib.DTYPE_FLOAT16, _stream_ptr(q.device))
+            _lib.DTYPE_FLOAT16, _stream_ptr(q.device), int(impl))
     _lib.check(rc, "prefill_attention")
     return out
 

@@ -64,6 +64,13 @@ typedef enum {
   PDB_IMPL_TMA_STATIC = 5 /* TMA-fed tensor cores, static schedule only       */
 } pdb_impl_t;
 
+/* Kernel selection for pdb_prefill_attention_impl. */
+typedef enum {
+  PDB_PREFILL_AUTO = 0,    /* tcgen05 kernel when block_size % 16 == 0, else mma.sync */
+  PDB_PREFILL_TCGEN05 = 1, /* TMA-staged tiles, tcgen05.mma with TMEM accumulators   */
+  PDB_PREFILL_MMA = 2      /* cp.async-staged tiles, mma.sync, any block size        */
+} pdb_prefill_impl_t;
+
 /* Bits of the per-device error word (pdb_read_device_errors). */
 #define PDB_DEVERR_TABLE_ENTRY 0x1u  /* block-table entry outside [0, num_blocks) */
 #define PDB_DEVERR_LENGTH 0x2u       /* length < 0 or > table_width*block_size   */
@@ -296,6 +303,15 @@ PDB_API int pdb_prefill_attention(const void* q, const void* k_pool, const void*
                                   int64_t batch, int64_t width, int64_t heads, int64_t head_dim,
                                   int64_t num_blocks, int64_t block_size, int64_t kv_heads,
                                   int64_t table_width, int dtype, void* stream);
+
+/* pdb_prefill_attention with the kernel pinned (pdb_prefill_impl_t); same
+ * results within FP16 rounding. PDB_PREFILL_TCGEN05 needs block_size % 16 == 0. */
+PDB_API int pdb_prefill_attention_impl(const void* q, const void* k_pool, const void* v_pool,
+                                       const int32_t* tables, const int32_t* lengths, void* out,
+                                       int64_t batch, int64_t width, int64_t heads,
+                                       int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                       int64_t kv_heads, int64_t table_width, int dtype,
+                                       void* stream, int impl);
 
 /*
  * Host-side copy of the default FP16 kernel's worker partition, for tests.

@@ -3,6 +3,10 @@ K/V read from the paged pools) against the reference's prefill attention
 (worker/llama.py:141-144, restated in oracle/paged_attention.py:
 repeat_interleave + causal SDPA over the padded batch, fp32).
 
+Both kernels are checked, pinned by `impl`: the tcgen05 kernel (TMA-staged
+tiles, tcgen05.mma with TMEM accumulators; block_size % 16 == 0) and the
+mma.sync kernel (cp.async tiles, any block size).
+
 Bars: rows of real tokens within 2e-3 (FP16); rows at or beyond a prompt's
 length exactly zero; pages placed in a fragmented pool through the tables."""
 from __future__ import annotations
@@ -19,7 +23,14 @@ pytestmark = pytest.mark.gpu
 W = import_module("workloads")
 
 
-def make_case(lengths, H, KVH, D, bs=16, seed=0, width=None, extra_blocks=37):
+IMPLS = pytest.mark.parametrize("impl", ["tcgen05", "mma"])
+
+
+def _impl(pkg, name):
+    return {"tcgen05": pkg.PREFILL_TCGEN05, "mma": pkg.PREFILL_MMA}[name]
+
+
+def make_case(lengths, H, KVH, D, bs=16, seed=0, width=None, extra_blocks=37, stale_nan=False):
     g = torch.Generator().manual_seed(seed)
     B = len(lengths)
     Wd = width or max(lengths)
@@ -37,6 +48,9 @@ def make_case(lengths, H, KVH, D, bs=16, seed=0, width=None, extra_blocks=37):
         off += n
     k_pool = (torch.randn(N, bs, KVH, D, generator=g) * 3).half()  # stale everywhere
     v_pool = (torch.randn(N, bs, KVH, D, generator=g) * 3).half()
+    if stale_nan:  # rows no prompt owns are NaN: they must never reach an output
+        k_pool.fill_(float("nan"))
+        v_pool.fill_(float("nan"))
     valid = torch.arange(Wd)[None, :] < lens[:, None]
     phys, offs = [], []
     for b, n in enumerate(lengths):
@@ -49,28 +63,77 @@ def make_case(lengths, H, KVH, D, bs=16, seed=0, width=None, extra_blocks=37):
     return q, k, v, k_pool, v_pool, tables, lens, valid
 
 
-@pytest.mark.parametrize("H,KVH,D", [(9, 3, 64), (32, 8, 128), (4, 4, 64), (8, 1, 128)])
-def test_prefill_attention_matches_reference(pkg, cuda, H, KVH, D):
-    lengths = [1, 63, 64, 65, 130, 200, 17, 128]
-    q, k, v, kp, vp, tables, lens, valid = make_case(lengths, H, KVH, D, seed=D + H)
-    out = pkg.prefill_attention(q.to(cuda), kp.to(cuda), vp.to(cuda), tables.to(cuda),
-                                lens.to(cuda)).cpu()
+def run(pkg, cuda, case, impl="tcgen05"):
+    q, k, v, kp, vp, tables, lens, valid = case
+    return pkg.prefill_attention(q.to(cuda), kp.to(cuda), vp.to(cuda), tables.to(cuda),
+                                 lens.to(cuda), impl=_impl(pkg, impl)).cpu()
+
+
+def check(out, case, what):
+    q, k, v, kp, vp, tables, lens, valid = case
     ref = opa.prefill_attention(q, k, v)
-    assert_parity(out[valid], ref[valid].half(), f"prefill H={H} KVH={KVH} D={D}")
+    assert_parity(out[valid], ref[valid].half(), what)
     assert torch.equal(out[~valid], torch.zeros_like(out[~valid]))
+
+
+@IMPLS
+@pytest.mark.parametrize("H,KVH,D", [(9, 3, 64), (32, 8, 128), (4, 4, 64), (8, 1, 128)])
+def test_prefill_attention_matches_reference(pkg, cuda, impl, H, KVH, D):
+    lengths = [1, 63, 64, 65, 130, 200, 17, 128]
+    case = make_case(lengths, H, KVH, D, seed=D + H)
+    check(run(pkg, cuda, case, impl), case, f"prefill {impl} H={H} KVH={KVH} D={D}")
     assert pkg.read_device_errors() == 0
 
 
-def test_prefill_attention_cfg4_prompts(pkg, cuda):
+@IMPLS
+def test_prefill_attention_cfg4_prompts(pkg, cuda, impl):
     """16 SmolLM2-shaped prompts, lengths U[64, 1024], padded to the longest."""
     g = torch.Generator().manual_seed(4)
     lengths = torch.randint(64, 1025, (16,), generator=g).tolist()
-    q, k, v, kp, vp, tables, lens, valid = make_case(lengths, 9, 3, 64, seed=44)
+    case = make_case(lengths, 9, 3, 64, seed=44)
+    check(run(pkg, cuda, case, impl), case, f"cfg4 prefill {impl}")
+
+
+@IMPLS
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_attention_ignores_nan_stale_rows(pkg, cuda, impl, D):
+    """Every pool row no prompt wrote is NaN: partial 16-token units and the
+    rest of each last page are staged but must not reach any output row."""
+    lengths = [5, 129, 255, 0, 300, 16]
+    case = make_case(lengths, 8, 2, D, seed=7 + D, width=320, stale_nan=True)
+    out = run(pkg, cuda, case, impl)
+    assert not torch.isnan(out).any()
+    check(out, case, f"NaN-stale prefill {impl} D={D}")
+    assert pkg.read_device_errors() == 0
+
+
+@pytest.mark.parametrize("bs", [32, 64])
+def test_prefill_attention_tcgen05_block_sizes(pkg, cuda, bs):
+    lengths = [31, 32, 33, 257, 96, 1]
+    case = make_case(lengths, 6, 2, 64, bs=bs, seed=bs)
+    check(run(pkg, cuda, case, "tcgen05"), case, f"tcgen05 prefill bs={bs}")
+
+
+def test_prefill_attention_block_size_8_takes_mma(pkg, cuda):
+    """block_size 8 splits a 16-token unit over two pages: the default picks
+    the mma.sync kernel, and pinning the tcgen05 kernel is refused."""
+    lengths = [9, 40, 77]
+    case = make_case(lengths, 4, 2, 64, bs=8, seed=8)
+    q, k, v, kp, vp, tables, lens, valid = case
     out = pkg.prefill_attention(q.to(cuda), kp.to(cuda), vp.to(cuda), tables.to(cuda),
                                 lens.to(cuda)).cpu()
-    ref = opa.prefill_attention(q, k, v)
-    assert_parity(out[valid], ref[valid].half(), "cfg4 prefill")
-    assert torch.equal(out[~valid], torch.zeros_like(out[~valid]))
+    check(out, case, "bs=8 prefill (auto)")
+    with pytest.raises(RuntimeError, match="block_size % 16"):
+        run(pkg, cuda, case, "tcgen05")
+
+
+def test_prefill_attention_kernels_agree(pkg, cuda):
+    """The two kernels round P to FP16 alike: results within FP16 rounding."""
+    lengths = [700, 513, 64, 1000]
+    case = make_case(lengths, 9, 3, 64, seed=99)
+    a = run(pkg, cuda, case, "tcgen05")
+    b = run(pkg, cuda, case, "mma")
+    torch.testing.assert_close(a, b, rtol=0, atol=2e-3)
 
 
 def test_prefill_attention_rejects_unsupported_shapes(pkg, cuda):
