@@ -897,6 +897,7 @@ int pdb_prefill_attention_impl(const void* q, const void* k_pool, const void* v_
     p.bs_shift = bs_shift;
     p.num_blocks = num_blocks;
     p.scale_log2 = scale_log2;
+    p.TZ = (int)((width + pdb::PrefillTc<64>::BM - 1) / pdb::PrefillTc<64>::BM);
     CUtensorMap qmap, kmap, vmap;
     if (!(encode_rows_map(&qmap, q, batch * width, heads, head_dim, pdb::PrefillTc<64>::BM) &&
           encode_pool_map(&kmap, k_pool, num_blocks, block_size, kv_heads, head_dim) &&
@@ -905,16 +906,28 @@ int pdb_prefill_attention_impl(const void* q, const void* k_pool, const void* v_
     const void* fn = head_dim == 64 ? reinterpret_cast<const void*>(&pdb::prefill_tc_kernel<64>)
                                     : reinterpret_cast<const void*>(&pdb::prefill_tc_kernel<128>);
     const size_t smem = head_dim == 64 ? pdb::PrefillTc<64>::SMEM : pdb::PrefillTc<128>::SMEM;
+    // Two CTAs per SM need the largest shared-memory carveout, which the
+    // driver does not pick by itself (a per-function preference).
+    static bool carveout_set[2] = {false, false};
+    if (!carveout_set[head_dim == 128]) {
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+        cudaGetLastError();
+      carveout_set[head_dim == 128] = true;
+    }
     // Each resident CTA holds 256 TMEM columns: at most two fit an SM's 512.
     constexpr int NT = pdb::PrefillTc<64>::NT;
     static_assert(NT == pdb::PrefillTc<128>::NT, "one block size");
-    const int occ = ctas_per_sm(dev, fn, smem, NT);
-    if (occ <= 0 || occ > 2)
-      return fail(PDB_ERR_CUDA, "tcgen05 prefill kernel residency is not 1-2 CTAs per SM");
-    // (query head, prompt, 128-row tile); the kernel maps blockIdx.z to tiles
-    // from the last one down, so the longest tiles are dispatched first.
-    const dim3 grid((unsigned)heads, (unsigned)batch,
-                    (unsigned)((width + pdb::PrefillTc<64>::BM - 1) / pdb::PrefillTc<64>::BM));
+    if (ctas_per_sm(dev, fn, smem, NT) <= 0)
+      return fail(PDB_ERR_CUDA, "tcgen05 prefill kernel cannot be resident");
+    // Persistent grid of two CTAs per SM, or one CTA per item if fewer. Two
+    // fit by registers (128 x 192 threads each), shared memory (with the
+    // largest carveout) and TMEM (256 columns each); the runtime's occupancy
+    // query answers 1 for tcgen05 kernels. CTAs never wait on one another, so
+    // a grid larger than what is resident is still correct.
+    const int64_t items = heads * batch * p.TZ;
+    const int64_t slots = 2 * (int64_t)sm_count(dev);
+    const dim3 grid((unsigned)(items < slots ? items : slots));
     if (head_dim == 64)
       e = launch_pdl(pdb::prefill_tc_kernel<64>, grid, dim3(NT), smem, st, p, qmap, kmap, vmap);
     else
