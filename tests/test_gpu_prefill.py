@@ -144,3 +144,43 @@ def test_prefill_attention_rejects_unsupported_shapes(pkg, cuda):
         pkg.prefill_attention(q, kp, kp, t, t[:, 0].contiguous())
     with pytest.raises(RuntimeError, match="FP16"):
         pkg.prefill_attention(q.float(), kp.float(), kp.float(), t, t[:, 0].contiguous())
+
+
+@pytest.mark.parametrize("B,seed", [(40, 5), (600, 6)])
+def test_prefill_attention_tcgen05_many_prompts(pkg, cuda, B, seed):
+    """More prompts than one warp ballot covers (40), and more than the
+    kernel keeps in shared memory (600 > 512: lengths read from global
+    memory); lengths include 0 and the full width, so every schedule phase
+    (working tiles by level, padding tiles) is crossed by many CTAs."""
+    g = torch.Generator().manual_seed(seed)
+    hi = 300 if B == 40 else 70
+    lengths = torch.randint(0, hi + 1, (B,), generator=g).tolist()
+    lengths[0], lengths[-1] = 0, hi
+    case = make_case(lengths, 4, 2, 64, seed=seed, width=hi, extra_blocks=5)
+    check(run(pkg, cuda, case, "tcgen05"), case, f"tcgen05 prefill B={B}")
+    assert pkg.read_device_errors() == 0
+
+
+def test_prefill_attention_tcgen05_repeated_calls_and_graph(pkg, cuda):
+    """The persistent kernel carries no state between launches: eager calls
+    with different batches on one stream and replays of a captured call all
+    match the oracle."""
+    cases = [make_case([130, 7, 300], 6, 3, 64, seed=21),
+             make_case([1000, 3], 6, 3, 64, seed=22)]
+    for case in cases * 2:
+        check(run(pkg, cuda, case, "tcgen05"), case, "eager")
+    q, k, v, kp, vp, tables, lens, valid = cases[0]
+    dq, dk, dvp = q.to(cuda), kp.to(cuda), vp.to(cuda)
+    dt, dl = tables.to(cuda), lens.to(cuda)
+    out = torch.empty_like(dq)
+    s = torch.cuda.Stream(cuda)
+    with torch.cuda.stream(s):
+        pkg.prefill_attention(dq, dk, dvp, dt, dl, out=out)  # warm-up outside capture
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=s):
+            pkg.prefill_attention(dq, dk, dvp, dt, dl, out=out)
+    for _ in range(3):
+        out.zero_()
+        gr.replay()
+        torch.cuda.synchronize()
+        check(out.cpu(), cases[0], "graph replay")
