@@ -523,7 +523,7 @@ def run_ours(args):
             "achieved_gbs_step": full.seq_step_bytes() / (ms_step * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": ATTN_KERNEL if step.fused else ATTN_KERNEL_TWO,
+                         "kernel": attn_kernel_label(w.head_dim, step.fused),
                          "peak_source": f"{peak_src} hbm_gbs",
                          "algorithmic_bytes_per_launch": attn_bytes,
                          "ms_per_launch": ms_attn, "prologue_ms_per_launch": ms_pro,
@@ -543,12 +543,16 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# The kernel a decode layer launches for the FP16, head_dim 128, GQA-4 workload
-ATTN_KERNEL = ("attn_tma_dyn_kernel<MmaMath<128,4,3,TMA>, fused prologue>: RoPE + KV-slot "
-               "write + attention, TMA producer warp, tensor-core stream-K, dynamic tail, "
-               "epilogue warp")
-ATTN_KERNEL_TWO = ("attn_tma_dyn_kernel<MmaMath<128,4,3,TMA>>: TMA producer warp, tensor-core "
-                   "stream-K, dynamic tail, epilogue warp")
+# The kernel a decode layer launches for an FP16 workload with GQA group <= 4
+# (head_dim 128: 64-token tiles; head_dim 64: 128-token tiles, two 16-token
+# blocks per warp).
+def attn_kernel_label(head_dim: int, fused: bool) -> str:
+    m = "MmaMath<128,4,3,TMA>" if head_dim == 128 else f"MmaMath<{head_dim},4,3,TMA,2>"
+    if fused:
+        return (f"attn_tma_dyn_kernel<{m}, fused prologue>: RoPE + KV-slot write + attention, "
+                "TMA producer warp, tensor-core stream-K, dynamic tail, epilogue warp")
+    return (f"attn_tma_dyn_kernel<{m}>: TMA producer warp, tensor-core stream-K, dynamic "
+            "tail, epilogue warp")
 
 
 def run_reference(args):
