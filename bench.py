@@ -200,7 +200,8 @@ class DecodeStep:
         if self.fused:
             PKG.decode_attention(t.q[layer], t.k[layer], t.v[layer], t.k_pools[layer],
                                  t.v_pools[layer], t.tables, t.lengths, t.inv_freq,
-                                 self.w.max_length, out=self.out[layer])
+                                 self.w.max_length, out=self.out[layer],
+                                 metadata_stable=layer > 0)
         else:
             self.prologue(layer)
             self.attention(layer)
@@ -290,7 +291,7 @@ def e2e_run(w, t, steps, warmup, device):
             if fused:
                 PKG.decode_attention(d_q[layer], d_k[layer], d_v[layer], t.k_pools[layer],
                                      t.v_pools[layer], tables, lengths, t.inv_freq,
-                                     w.max_length, out=d_out[layer])
+                                     w.max_length, out=d_out[layer], metadata_stable=layer > 0)
             else:
                 positions, physical, offsets = d_meta[2:]
                 PKG.rope_kv_write(d_q[layer], d_k[layer], d_v[layer], t.k_pools[layer],

@@ -40,6 +40,10 @@ SIGNATURES = {
                                       _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                       _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_ptr,
                                       _c_size, _c_ptr]),
+    "pdb_decode_attention_ex": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                         _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                         _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_ptr,
+                                         _c_size, _c_ptr, ctypes.c_uint]),
     "pdb_decode_attention_supported": (_c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                                 _c_int]),
     "pdb_prefill_attention": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64,
@@ -62,6 +66,7 @@ DTYPE_FLOAT32 = 0
 DTYPE_FLOAT16 = 1
 IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA, IMPL_TMA_STATIC = 0, 1, 2, 3, 4, 5
 PREFILL_AUTO, PREFILL_TCGEN05, PREFILL_MMA = 0, 1, 2
+DECODE_STABLE_METADATA = 0x1
 STATUS_NAMES = {0: "ok", 1: "invalid argument", 2: "workspace", 3: "cuda"}
 
 _lock = threading.Lock()

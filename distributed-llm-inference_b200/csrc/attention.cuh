@@ -69,6 +69,11 @@ struct AttnParams {
   const void* k_new;
   const void* v_new;
   const float* inv_freq;
+  // Fused decode only: the caller guarantees that tables, lengths and
+  // inv_freq are not written by the previous kernel in the stream (true for
+  // every layer after the first of a decode step), so the launch may read them
+  // (plan, page lookups) before its programmatic-dependent-launch wait.
+  int stable_meta;
   int64_t q_row;   // fused: elements between consecutive sequences' q rows (H * D if packed)
   int64_t kv_row;  // fused: same for k_new / v_new (KVH * D if packed)
 };

@@ -422,17 +422,27 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
     fence_barrier_init();
   }
   launch_dependents();
-  grid_dependency_wait();  // every global access comes after this
+  // Every global access that may see the previous kernel's writes comes after
+  // grid_dependency_wait(). With stable metadata (fused decode, layers after
+  // the first of a step) the plan and the producer's page lookups read only
+  // tables, lengths and inv_freq, so they run before it, overlapping the
+  // previous launch's tail: each role then waits right before its first
+  // access to q, the pools, the output or the workspace.
+  const bool early = FUSE && p.stable_meta != 0;
+  if (!early) grid_dependency_wait();
   if constexpr (FUSE) {
     for (int i = tid; i < D / 2; i += NT) invf[i] = __ldg(p.inv_freq + i);
   }
   static_assert(3 + 3 * (NT / 32) <= kDynMisc, "plan scratch");
   DynPlan pl;
   const int64_t U = plan_dyn_stream<NT>(p, P, Ls, ord, misc, gridDim.x, TU, pl);
-  for (int i = blockIdx.x; i < p.B; i += gridDim.x) {
-    if (Ls[i] == 0) {
-      T* o = static_cast<T*>(p.out) + (int64_t)ord[i] * p.H * D;
-      for (int j = tid; j < p.H * D; j += NT) o[j] = Elem<T>::from_f(0.f);
+  if (early && warp != NW) grid_dependency_wait();  // math and epilogue warps
+  if (warp < NW) {  // zero rows of empty sequences (the producer warp may not have waited)
+    for (int i = blockIdx.x; i < p.B; i += gridDim.x) {
+      if (Ls[i] == 0) {
+        T* o = static_cast<T*>(p.out) + (int64_t)ord[i] * p.H * D;
+        for (int j = tid; j < p.H * D; j += NW * 32) o[j] = Elem<T>::from_f(0.f);
+      }
     }
   }
   if (U == 0) return;
@@ -449,9 +459,17 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
       const uint32_t use = (uint32_t)(k / STAGES);
       if (use > 0) mbar_wait(&empty[s], (use - 1) & 1);
     };
+    bool waited = !early;  // producer: wait before the first claim or TMA
+    auto wait_prev = [&]() {
+      if (!waited) {
+        grid_dependency_wait();
+        waited = true;
+      }
+    };
     // Tail chunks are claimed when the last tile of the current worker has
     // been issued, i.e. STAGES tiles before the math warps run out of work.
     auto claim = [&]() -> int64_t {
+      wait_prev();
       int64_t c = pl.K;
       if (pl.K > 0 && lane == 0) c = claim_chunk(claim_ctr, p.call_tag, pl.K, gridDim.x);
       return __shfl_sync(0xffffffffu, c, 0);
@@ -529,6 +547,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
                                      : -1;
           }
         }
+        wait_prev();
         if (lane == 0) {
           fence_proxy_async_smem();
           mbar_arrive_expect_tx(&full[s], (uint32_t)__popc(okmask) * K::UNIT_BYTES);

@@ -797,6 +797,20 @@ int pdb_decode_attention(const void* q, const void* k_new, const void* v_new, vo
                          int64_t N, int64_t bs, int64_t KVH, int64_t W, int64_t max_length,
                          int64_t q_row_stride, int64_t kv_row_stride, int dtype,
                          void* workspace, size_t workspace_bytes, void* stream) {
+  return pdb_decode_attention_ex(q, k_new, v_new, k_pool, v_pool, tables, lengths, inv_freq, out,
+                                 B, H, D, N, bs, KVH, W, max_length, q_row_stride, kv_row_stride,
+                                 dtype, workspace, workspace_bytes, stream, 0u);
+}
+
+int pdb_decode_attention_ex(const void* q, const void* k_new, const void* v_new, void* k_pool,
+                            void* v_pool, const int32_t* tables, const int32_t* lengths,
+                            const float* inv_freq, void* out, int64_t B, int64_t H, int64_t D,
+                            int64_t N, int64_t bs, int64_t KVH, int64_t W, int64_t max_length,
+                            int64_t q_row_stride, int64_t kv_row_stride, int dtype,
+                            void* workspace, size_t workspace_bytes, void* stream,
+                            unsigned flags) {
+  if (flags & ~(unsigned)PDB_DECODE_STABLE_METADATA)
+    return fail(PDB_ERR_INVALID_ARGUMENT, "unknown decode attention flags");
   int rc = check_attention_args(B, H, D, N, bs, KVH, D, W, max_length, dtype);
   if (rc) return rc;
   if (!q || !k_new || !v_new || !k_pool || !v_pool || !tables || !lengths || !inv_freq || !out)
@@ -837,6 +851,7 @@ int pdb_decode_attention(const void* q, const void* k_new, const void* v_new, vo
   p.k_new = k_new;
   p.v_new = v_new;
   p.inv_freq = inv_freq;
+  p.stable_meta = (flags & PDB_DECODE_STABLE_METADATA) ? 1 : 0;
   p.q_row = q_row;
   p.kv_row = kv_row;
   CUtensorMap kmap, vmap;

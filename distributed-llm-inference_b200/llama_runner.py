@@ -142,7 +142,8 @@ def _tick(runner, cache, token_tensor, tables, lengths, max_length):
             k = qkv[:, H * D:(H + KVH) * D].view(batch, KVH, D)
             v = qkv[:, (H + KVH) * D:].view(batch, KVH, D)
             context = decode_attention(q, k, v, cache.keys[index], cache.values[index], tables,
-                                       lengths, runner.inv_freq, max_length)
+                                       lengths, runner.inv_freq, max_length,
+                                       metadata_stable=index > 0)
             x2 = torch.addmm(x2, context.view(batch, -1), attn.o_proj.weight.t())
             gu = F.linear(_rms_norm(layer.post_attention_layernorm, x2), wgu)
             inter = wgu.shape[0] // 2
@@ -157,7 +158,8 @@ def _tick(runner, cache, token_tensor, tables, lengths, max_length):
         v = attn.v_proj(normalized).view(batch, runner.kv_heads, runner.head_dim)
         if fused:
             context = decode_attention(q, k, v, cache.keys[index], cache.values[index], tables,
-                                       lengths, runner.inv_freq, max_length)
+                                       lengths, runner.inv_freq, max_length,
+                                       metadata_stable=index > 0)
         else:
             q, k = rope_kv_write_decode(q, k, v, cache.keys[index], cache.values[index],
                                         tables, lengths, runner.inv_freq,

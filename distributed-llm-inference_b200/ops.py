@@ -278,7 +278,8 @@ def decode_attention_supported(q: torch.Tensor, k_pool: torch.Tensor) -> bool:
 def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor,
                      v_pool: torch.Tensor, tables: torch.Tensor, lengths: torch.Tensor,
                      inv_freq: torch.Tensor, max_length: int, *,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
+                     out: torch.Tensor | None = None,
+                     metadata_stable: bool = False) -> torch.Tensor:
     """One decode layer in one launch (worker/llama.py:168-174).
 
     ``rope_kv_write_decode(..., advance=False)`` followed by
@@ -289,6 +290,11 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
     and v are written to the token's slot; returns the attention output
     [B, H, D], bit-identical to the two-launch path. FP16 only (see
     ``decode_attention_supported``).
+
+    ``metadata_stable=True`` promises that tables, lengths and inv_freq were
+    not written by the previous kernel on the stream (every layer after the
+    first of a decode step): the launch then plans its work and looks up
+    pages while that kernel is still finishing. Results are identical.
     """
     # q, k and v may be row slices of one fused projection output: heads packed
     # within a sequence (strides (row, D, 1)), any row stride between sequences
@@ -316,12 +322,12 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
         stream = _stream_ptr(q.device)
         need = lib.pdb_paged_attention_workspace_size(B, H, KVH, D, int(max_length), dt)
         ws = workspace(q.device, stream, need, "attention")
-        rc = lib.pdb_decode_attention(
+        rc = lib.pdb_decode_attention_ex(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
             tables.data_ptr(), lengths.data_ptr(), inv_freq.data_ptr(), out.data_ptr(), B, H, D,
             N, bs, KVH, tables.size(1), int(max_length), q.stride(0), k.stride(0), dt,
             ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-            stream)
+            stream, _lib.DECODE_STABLE_METADATA if metadata_stable else 0)
     _lib.check(rc, "decode_attention")
     return out
 

@@ -277,6 +277,24 @@ PDB_API int pdb_decode_attention(const void* q, const void* k_new, const void* v
                                  int64_t q_row_stride, int64_t kv_row_stride, int dtype,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* Flags of pdb_decode_attention_ex. */
+#define PDB_DECODE_STABLE_METADATA 0x1u /* tables, lengths and inv_freq are not written by
+                                           the previous kernel in the stream (every layer
+                                           after the first of a decode step): the launch
+                                           plans its work and looks up pages while that
+                                           kernel finishes (programmatic dependent launch) */
+
+/* pdb_decode_attention with flags (0 = pdb_decode_attention). */
+PDB_API int pdb_decode_attention_ex(const void* q, const void* k_new, const void* v_new,
+                                    void* k_pool, void* v_pool, const int32_t* tables,
+                                    const int32_t* lengths, const float* inv_freq, void* out,
+                                    int64_t batch, int64_t heads, int64_t head_dim,
+                                    int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                                    int64_t table_width, int64_t max_length,
+                                    int64_t q_row_stride, int64_t kv_row_stride, int dtype,
+                                    void* workspace, size_t workspace_bytes, void* stream,
+                                    unsigned flags);
+
 /* 1 when pdb_decode_attention covers this shape on the current device, else 0. */
 PDB_API int pdb_decode_attention_supported(int64_t batch, int64_t heads, int64_t kv_heads,
                                            int64_t head_dim, int64_t num_blocks,

@@ -309,3 +309,61 @@ def test_fused_decode_layer_reads_projection_slices(pkg, cuda):
     assert torch.equal(a, b)
     assert torch.equal(kp1, kp2) and torch.equal(vp1, vp2)
     assert pkg.read_device_errors() == 0
+
+
+@pytest.mark.parametrize("shape", ["llama3", "smollm"])
+def test_fused_decode_stable_metadata_is_identical(pkg, cuda, shape):
+    """A decode step of 4 layers launched back to back with
+    metadata_stable=True for layers 1..3 (plan and page lookups before the
+    dependent-launch wait) gives the same outputs and pool bytes as the
+    same step without it, eagerly and replayed from a CUDA graph."""
+    if shape == "llama3":
+        w = W.llama3_8b(batch=40, layers=4)
+    else:
+        w = W.smollm_fp16(batch=64, layers=4)
+    t = W.materialize(w, cuda)
+    pools0 = [(kp.clone(), vp.clone()) for kp, vp in zip(t.k_pools, t.v_pools)]
+
+    def step(stable, outs):
+        for layer in range(w.layers):
+            pkg.decode_attention(t.q[layer], t.k[layer], t.v[layer], t.k_pools[layer],
+                                 t.v_pools[layer], t.tables, t.lengths, t.inv_freq,
+                                 w.max_length, out=outs[layer],
+                                 metadata_stable=stable and layer > 0)
+
+    def reset():  # on the current stream, then complete before the step's stream runs
+        for (kp, vp), (k0, v0) in zip(zip(t.k_pools, t.v_pools), pools0):
+            kp.copy_(k0)
+            vp.copy_(v0)
+        torch.cuda.synchronize()
+
+    ref = [torch.empty_like(q) for q in t.q]
+    got = [torch.empty_like(q) for q in t.q]
+    s = torch.cuda.Stream(cuda)
+    with torch.cuda.stream(s):
+        step(False, ref)
+    torch.cuda.synchronize()
+    ref_pools = [(kp.clone(), vp.clone()) for kp, vp in zip(t.k_pools, t.v_pools)]
+    reset()
+    with torch.cuda.stream(s):
+        step(True, got)
+    torch.cuda.synchronize()
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    for (kp, vp), (kr, vr) in zip(zip(t.k_pools, t.v_pools), ref_pools):
+        assert torch.equal(kp, kr) and torch.equal(vp, vr)
+    # graph capture of the stable-metadata step, replayed
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        step(True, got)
+    for _ in range(3):
+        reset()
+        for o in got:
+            o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)
+        for (kp, vp), (kr, vr) in zip(zip(t.k_pools, t.v_pools), ref_pools):
+            assert torch.equal(kp, kr) and torch.equal(vp, vr)
+    assert pkg.read_device_errors() == 0
