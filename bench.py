@@ -201,7 +201,7 @@ class DecodeStep:
             PKG.decode_attention(t.q[layer], t.k[layer], t.v[layer], t.k_pools[layer],
                                  t.v_pools[layer], t.tables, t.lengths, t.inv_freq,
                                  self.w.max_length, out=self.out[layer],
-                                 metadata_stable=layer > 0)
+                                 metadata_stable=layer > 0, pools_stable=layer > 0)
         else:
             self.prologue(layer)
             self.attention(layer)
@@ -291,7 +291,8 @@ def e2e_run(w, t, steps, warmup, device):
             if fused:
                 PKG.decode_attention(d_q[layer], d_k[layer], d_v[layer], t.k_pools[layer],
                                      t.v_pools[layer], tables, lengths, t.inv_freq,
-                                     w.max_length, out=d_out[layer], metadata_stable=layer > 0)
+                                     w.max_length, out=d_out[layer], metadata_stable=layer > 0,
+                                     pools_stable=layer > 0)
             else:
                 positions, physical, offsets = d_meta[2:]
                 PKG.rope_kv_write(d_q[layer], d_k[layer], d_v[layer], t.k_pools[layer],

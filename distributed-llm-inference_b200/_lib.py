@@ -67,6 +67,7 @@ DTYPE_FLOAT16 = 1
 IMPL_AUTO, IMPL_FAST, IMPL_GENERIC, IMPL_SIMT, IMPL_MMA, IMPL_TMA_STATIC = 0, 1, 2, 3, 4, 5
 PREFILL_AUTO, PREFILL_TCGEN05, PREFILL_MMA = 0, 1, 2
 DECODE_STABLE_METADATA = 0x1
+DECODE_STABLE_POOLS = 0x2
 STATUS_NAMES = {0: "ok", 1: "invalid argument", 2: "workspace", 3: "cuda"}
 
 _lock = threading.Lock()

@@ -70,9 +70,10 @@ struct AttnParams {
   const void* v_new;
   const float* inv_freq;
   // Fused decode only: the caller guarantees that tables, lengths and
-  // inv_freq are not written by the previous kernel in the stream (true for
-  // every layer after the first of a decode step), so the launch may read them
-  // (plan, page lookups) before its programmatic-dependent-launch wait.
+  // inv_freq (bit 0) and also the KV pools (bit 1) are not written by the
+  // previous kernel in the stream (true for every layer after the first of a
+  // fused decode step), so the launch may read them (plan, page lookups; K/V
+  // tiles) before its programmatic-dependent-launch wait.
   int stable_meta;
   int64_t q_row;   // fused: elements between consecutive sequences' q rows (H * D if packed)
   int64_t kv_row;  // fused: same for k_new / v_new (KVH * D if packed)

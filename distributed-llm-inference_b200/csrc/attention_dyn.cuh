@@ -426,9 +426,12 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
   // grid_dependency_wait(). With stable metadata (fused decode, layers after
   // the first of a step) the plan and the producer's page lookups read only
   // tables, lengths and inv_freq, so they run before it, overlapping the
-  // previous launch's tail: each role then waits right before its first
-  // access to q, the pools, the output or the workspace.
-  const bool early = FUSE && p.stable_meta != 0;
+  // previous launch's tail; with stable pools as well the producer's K/V
+  // tiles are loaded before it too. Each role waits right before its first
+  // access to anything else (q, new k/v, the output, the workspace counters;
+  // the pools when they are not stable).
+  const bool early = FUSE && (p.stable_meta & 1) != 0;
+  const bool early_kv = early && (p.stable_meta & 2) != 0;  // K/V tiles too
   if (!early) grid_dependency_wait();
   if constexpr (FUSE) {
     for (int i = tid; i < D / 2; i += NT) invf[i] = __ldg(p.inv_freq + i);
@@ -547,7 +550,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
                                      : -1;
           }
         }
-        wait_prev();
+        if (!early_kv) wait_prev();
         if (lane == 0) {
           fence_proxy_async_smem();
           mbar_arrive_expect_tx(&full[s], (uint32_t)__popc(okmask) * K::UNIT_BYTES);

@@ -809,8 +809,11 @@ int pdb_decode_attention_ex(const void* q, const void* k_new, const void* v_new,
                             int64_t q_row_stride, int64_t kv_row_stride, int dtype,
                             void* workspace, size_t workspace_bytes, void* stream,
                             unsigned flags) {
-  if (flags & ~(unsigned)PDB_DECODE_STABLE_METADATA)
+  if (flags & ~(unsigned)(PDB_DECODE_STABLE_METADATA | PDB_DECODE_STABLE_POOLS))
     return fail(PDB_ERR_INVALID_ARGUMENT, "unknown decode attention flags");
+  if ((flags & PDB_DECODE_STABLE_POOLS) && !(flags & PDB_DECODE_STABLE_METADATA))
+    return fail(PDB_ERR_INVALID_ARGUMENT,
+                "PDB_DECODE_STABLE_POOLS requires PDB_DECODE_STABLE_METADATA");
   int rc = check_attention_args(B, H, D, N, bs, KVH, D, W, max_length, dtype);
   if (rc) return rc;
   if (!q || !k_new || !v_new || !k_pool || !v_pool || !tables || !lengths || !inv_freq || !out)
@@ -851,7 +854,8 @@ int pdb_decode_attention_ex(const void* q, const void* k_new, const void* v_new,
   p.k_new = k_new;
   p.v_new = v_new;
   p.inv_freq = inv_freq;
-  p.stable_meta = (flags & PDB_DECODE_STABLE_METADATA) ? 1 : 0;
+  p.stable_meta = ((flags & PDB_DECODE_STABLE_METADATA) ? 1 : 0) |
+                  ((flags & PDB_DECODE_STABLE_POOLS) ? 2 : 0);
   p.q_row = q_row;
   p.kv_row = kv_row;
   CUtensorMap kmap, vmap;

@@ -279,7 +279,8 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
                      v_pool: torch.Tensor, tables: torch.Tensor, lengths: torch.Tensor,
                      inv_freq: torch.Tensor, max_length: int, *,
                      out: torch.Tensor | None = None,
-                     metadata_stable: bool = False) -> torch.Tensor:
+                     metadata_stable: bool = False,
+                     pools_stable: bool = False) -> torch.Tensor:
     """One decode layer in one launch (worker/llama.py:168-174).
 
     ``rope_kv_write_decode(..., advance=False)`` followed by
@@ -294,8 +295,13 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
     ``metadata_stable=True`` promises that tables, lengths and inv_freq were
     not written by the previous kernel on the stream (every layer after the
     first of a decode step): the launch then plans its work and looks up
-    pages while that kernel is still finishing. Results are identical.
+    pages while that kernel is still finishing. ``pools_stable=True``
+    (requires ``metadata_stable``) adds that k_pool and v_pool were not
+    written by it either — true when every layer of the step is one
+    decode_attention launch — and lets the first K/V tiles load early too.
+    Results are identical.
     """
+    _check(metadata_stable or not pools_stable, "pools_stable requires metadata_stable")
     # q, k and v may be row slices of one fused projection output: heads packed
     # within a sequence (strides (row, D, 1)), any row stride between sequences
     _check(q.is_cuda and q.dim() == 3 and q.stride(2) == 1 and q.stride(1) == q.size(2)
@@ -327,7 +333,8 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
             tables.data_ptr(), lengths.data_ptr(), inv_freq.data_ptr(), out.data_ptr(), B, H, D,
             N, bs, KVH, tables.size(1), int(max_length), q.stride(0), k.stride(0), dt,
             ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-            stream, _lib.DECODE_STABLE_METADATA if metadata_stable else 0)
+            stream, (_lib.DECODE_STABLE_METADATA if metadata_stable else 0)
+            | (_lib.DECODE_STABLE_POOLS if pools_stable else 0))
     _lib.check(rc, "decode_attention")
     return out
 

@@ -283,6 +283,11 @@ PDB_API int pdb_decode_attention(const void* q, const void* k_new, const void* v
                                            after the first of a decode step): the launch
                                            plans its work and looks up pages while that
                                            kernel finishes (programmatic dependent launch) */
+#define PDB_DECODE_STABLE_POOLS 0x2u    /* with STABLE_METADATA: k_pool and v_pool are not
+                                           written by the previous kernel either (every layer
+                                           after the first of a step of one-launch layers,
+                                           whose pools only their own launch writes): the
+                                           first K/V tiles are loaded while it finishes too */
 
 /* pdb_decode_attention with flags (0 = pdb_decode_attention). */
 PDB_API int pdb_decode_attention_ex(const void* q, const void* k_new, const void* v_new,

@@ -329,7 +329,8 @@ def test_fused_decode_stable_metadata_is_identical(pkg, cuda, shape):
             pkg.decode_attention(t.q[layer], t.k[layer], t.v[layer], t.k_pools[layer],
                                  t.v_pools[layer], t.tables, t.lengths, t.inv_freq,
                                  w.max_length, out=outs[layer],
-                                 metadata_stable=stable and layer > 0)
+                                 metadata_stable=stable and layer > 0,
+                                 pools_stable=stable and layer > 0)
 
     def reset():  # on the current stream, then complete before the step's stream runs
         for (kp, vp), (k0, v0) in zip(zip(t.k_pools, t.v_pools), pools0):
