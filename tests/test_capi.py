@@ -168,3 +168,25 @@ def test_dynamic_partition_covers_units(lib, units, launched):
     if len(tail):
         assert np.all(tail[:, 1] - tail[:, 0] >= 16)  # four 64-token tiles
         assert tail[0, 0] == units - units // 16
+
+
+def test_prefill_and_decode_selector_checks(lib):
+    """Kernel selectors and flags are validated before any CUDA call."""
+    args = [None] * 6 + [2, 8, 4, 64, 16, 16, 2, 1, 1, None]
+    assert lib.pdb_prefill_attention_impl(*args, 3) == 1
+    assert "unknown prefill kernel" in _lib.last_error()
+    assert lib.pdb_prefill_attention_impl(*args, -1) == 1
+    dec = [None] * 9 + [2, 4, 64, 16, 16, 2, 1, 16, 0, 0, 1, None, 0, None]
+    assert lib.pdb_decode_attention_ex(*dec, 4) == 1
+    assert "unknown decode attention flags" in _lib.last_error()
+    assert lib.pdb_decode_attention_ex(*dec, _lib.DECODE_STABLE_POOLS) == 1
+    assert "requires PDB_DECODE_STABLE_METADATA" in _lib.last_error()
+
+
+def test_prefill_ops_checks_without_device(pkg):
+    """prefill_attention rejects CPU tensors before reaching the library."""
+    q = torch.zeros(1, 4, 2, 64, dtype=torch.float16)
+    kp = torch.zeros(2, 16, 1, 64, dtype=torch.float16)
+    t = torch.zeros(1, 1, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pkg.prefill_attention(q, kp, kp, t, t[:, 0].contiguous())
