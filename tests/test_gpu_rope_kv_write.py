@@ -75,7 +75,7 @@ def test_decode_prologue_fp16(pkg, cuda, inplace):
     k_before, v_before = t.k_pools[0].cpu(), t.v_pools[0].cpu()
     q_in, k_in, v_in = t.q[0].clone(), t.k[0].clone(), t.v[0].clone()
     qr, kr = orope.rope(q_in.cpu().unsqueeze(1), k_in.cpu().unsqueeze(1), w.positions(),
-                        t.inv_freq.cpu())
+                        t.inv_freq.cpu(), exact_trig=True)
     qo, ko = pkg.rope_kv_write(t.q[0], t.k[0], t.v[0], t.k_pools[0], t.v_pools[0],
                                t.physical, t.offsets, t.positions, t.inv_freq, inplace=inplace)
     assert_parity(qo, qr[:, 0], "q")
@@ -99,7 +99,7 @@ def test_prefill_write(pkg, cuda):
     g = gold("prefill.pt")
     pw = W.prefill_smollm()
     d = W.materialize_prefill(pw, "cpu")
-    qr, kr = orope.rope(d["q"], d["k"], d["positions"], d["inv_freq"])
+    qr, kr = orope.rope(d["q"], d["k"], d["positions"], d["inv_freq"], exact_trig=True)
     dd = {k: v.to(cuda) for k, v in d.items()}
     qo, ko = pkg.rope_kv_write(dd["q"], dd["k"], dd["v"], dd["k_pool"], dd["v_pool"],
                                dd["physical"], dd["offsets"], dd["positions"], dd["inv_freq"],
@@ -130,7 +130,7 @@ def test_prologue_then_attention_llama3(pkg, cuda):
                                t.physical, t.offsets, t.positions, t.inv_freq)
     out = pkg.paged_attention(qo, t.k_pools[0], t.v_pools[0], t.tables, t.lengths, w.max_length)
     qr, kr = orope.rope(t.q[0].cpu().unsqueeze(1), t.k[0].cpu().unsqueeze(1), w.positions(),
-                        t.inv_freq.cpu())
+                        t.inv_freq.cpu(), exact_trig=True)
     assert_parity(qo, qr[:, 0], "q")
     assert_parity(ko, kr[:, 0], "k")
     from gpu_helpers import subset_pool
@@ -157,7 +157,7 @@ def test_rope_vector_and_scalar_paths(pkg, cuda, dtype, D):
     inv = W.inv_freq(1e4, D)
     pool_k = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
     pool_v = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
-    qr, kr = orope.rope(q, k, pos, inv)
+    qr, kr = orope.rope(q, k, pos, inv, exact_trig=True)
     kd, vd = pool_k.to(cuda), pool_v.to(cuda)
     qo, ko = pkg.rope_kv_write(q.to(cuda), k.to(cuda), v.to(cuda), kd, vd, phys.to(cuda),
                                off.to(cuda), pos.to(cuda), inv.to(cuda))

@@ -61,7 +61,7 @@ def test_rope_kv_write_decode(pkg, cuda, dtype, D, advance):
     pos = (lengths if advance else lengths - 1).to(torch.int64)
     phys = perm[torch.arange(B), (pos // bs)].to(torch.int64)
     off = pos % bs
-    qr, kr = orope.rope(q.unsqueeze(1), k.unsqueeze(1), pos[:, None], inv)
+    qr, kr = orope.rope(q.unsqueeze(1), k.unsqueeze(1), pos[:, None], inv, exact_trig=True)
     exp_k, exp_v = pk.clone(), pv.clone()
     kv_cache.write_decode(exp_k, phys, off, kr[:, 0])
     kv_cache.write_decode(exp_v, phys, off, v)
