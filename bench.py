@@ -25,6 +25,9 @@ the reference's PagedLlama.decode (restated in oracle/llama_model.py, pinned
 to its logits) with the reference's own CUDA attention kernel when it was
 built into oracle/_ref, else its torch path.
 
+Fourth workload, ``--workload prefill_write``: the prefill RoPE + paged KV
+write of the same 16 prompts (worker/llama.py:128-140), one layer per step.
+
 Third workload, ``--workload prefill``: the prefill attention of 16 prompts
 with lengths U[64, 1024] (SmolLM2 heads 9/3, head_dim 64, FP16), one layer
 per step. Ours: prefill_attention over the paged pools. Reference arm: the
@@ -62,7 +65,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16", "smollm_tick", "prefill"],
+    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16", "smollm_tick", "prefill",
+                                           "prefill_write"],
                     default="llama3_8b")
     ap.add_argument("--batch", type=int, default=None, help="override the workload batch")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling)")
@@ -902,10 +906,98 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_WRITE_METRIC = ("prefill RoPE + paged KV write prompt tokens/s per layer "
+                        "(16 prompts, len U[64,1024])")
+
+
+def run_prefill_write(args):
+    """Prefill RoPE + paged KV-slot write of one layer (worker/llama.py:128-140),
+    16 SmolLM2-shaped prompts padded to the longest, into a 4096-block pool.
+    Ours: rope_kv_write with the valid mask (one varlen launch). Reference
+    arm: the reference's torch steps on the same GPU — RoPE of the padded q/k
+    with every op in FP16 (worker/llama.py:108-117) and
+    pool[slots] = k[valid], v[valid] (:138-140); the valid rows' flat indices
+    are computed once, outside the timed steps."""
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pw = W.prefill_smollm()
+    d = W.materialize_prefill(pw, device)
+    B, Wd, H, D = d["q"].shape
+    KVH = d["k"].shape[2]
+    e = d["q"].element_size()
+    ntok = int(pw.lengths.sum())
+    nbytes = ((2 * B * Wd * H * D + 3 * B * Wd * KVH * D) * e  # read q, k, v; write q', k'
+              + 2 * ntok * KVH * D * e + B * Wd)                # k, v slot writes; mask
+    if args.impl == "reference":
+        vidx = d["valid"].reshape(-1).nonzero()[:, 0]
+        q_o, k_o = torch.empty_like(d["q"]), torch.empty_like(d["k"])
+
+        def rot(x):
+            a, b = x.chunk(2, dim=-1)
+            return torch.cat((-b, a), dim=-1)
+
+        def step():
+            f = d["positions"].float()[..., None] * d["inv_freq"]
+            ang = torch.cat((f, f), dim=-1)
+            cos = ang.cos().to(d["q"].dtype).unsqueeze(2)
+            sin = ang.sin().to(d["q"].dtype).unsqueeze(2)
+            torch.add(d["q"] * cos, rot(d["q"]) * sin, out=q_o)
+            torch.add(d["k"] * cos, rot(d["k"]) * sin, out=k_o)
+            d["k_pool"][d["physical"], d["offsets"]] = k_o.view(-1, KVH, D)[vidx]
+            d["v_pool"][d["physical"], d["offsets"]] = d["v"].view(-1, KVH, D)[vidx]
+        which = "reference prefill RoPE (torch ops in FP16) + index_put of the valid rows"
+    else:
+        q_o, k_o = torch.empty_like(d["q"]), torch.empty_like(d["k"])
+
+        def step():
+            PKG.rope_kv_write(d["q"], d["k"], d["v"], d["k_pool"], d["v_pool"], d["physical"],
+                              d["offsets"], d["positions"], d["inv_freq"], valid=d["valid"],
+                              q_out=q_o, k_out=k_o)
+        which = "rope_kv_write_vec_kernel + valid_scan_kernel (varlen scatter into the pages)"
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize(device)
+
+    def steps():  # the K timed steps back to back in one graph
+        for _ in range(args.steps):
+            step()
+    g = capture(steps, stream)
+    time_graph(g, 1, stream)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    ms = time_graph(g, 1, stream) / args.steps
+    clk = clocks.stop()
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
+        REPO / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs") or 6650.0
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    line = {"metric": PREFILL_WRITE_METRIC, "value": ntok / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic (seeded)",
+            "config": {"workload": "prefill RoPE + KV write: 16 prompts, len U[64,1024], heads "
+                                   "9/3, head_dim 64, block 16, 4096-block pool, one layer per step",
+                       "kernel": which, "prompt_tokens": ntok},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak, "traffic": None, "algorithmic_bytes_per_step": nbytes,
+                         "note": "padded q, k, v read and q', k' written; valid rows' k/v slots"},
+            "clocks": clk, "gpu_launches": 2 * args.steps if args.impl != "reference" else None}
+    if args.impl == "reference":
+        line["impl"] = "reference"
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "prefill_write":
+        run_prefill_write(args)
     elif args.workload == "smollm_tick":
         (run_tick_reference if args.impl == "reference" else run_tick)(args)
     elif args.impl == "reference":

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <type_traits>
 #include <mutex>
 #include <string>
 #include <tuple>
@@ -460,13 +461,24 @@ int launch_rope(const pdb::RopeParams& p, int dtype, cudaStream_t st) {
                       aligned16(p.v) && aligned16(p.q_out) && aligned16(p.k_out) &&
                       aligned16(p.k_pool) && aligned16(p.v_pool);
   if (vec_ok) {
-    constexpr int kRows = 2;
-    const unsigned grid = (unsigned)((p.num_rows + kRows - 1) / kRows);
-    const size_t smem = (size_t)kRows * p.dim * sizeof(float);
-    if (dtype == PDB_DTYPE_FLOAT16)
-      launch_pdl(pdb::rope_kv_write_vec_kernel<__half, kRows>, dim3(grid), dim3(256), smem, st, p);
+    // 16-byte work items of one row (q and k chunk pairs, v chunks): with few
+    // of them (small head counts) and many rows (prefill), 8 rows per CTA
+    // keep the 256 threads busy and amortise each CTA's set-up.
+    const int64_t per_row = (int64_t)(p.heads + 3 * p.kv_heads) * (p.dim / 2) * esize / 16;
+    const bool wide = p.num_rows >= 2048 && per_row <= 128;
+    auto go = [&](auto rows_tag) {
+      constexpr int kRows = decltype(rows_tag)::value;
+      const unsigned grid = (unsigned)((p.num_rows + kRows - 1) / kRows);
+      const size_t smem = (size_t)kRows * p.dim * sizeof(float);
+      if (dtype == PDB_DTYPE_FLOAT16)
+        launch_pdl(pdb::rope_kv_write_vec_kernel<__half, kRows>, dim3(grid), dim3(256), smem, st, p);
+      else
+        launch_pdl(pdb::rope_kv_write_vec_kernel<float, kRows>, dim3(grid), dim3(256), smem, st, p);
+    };
+    if (wide)
+      go(std::integral_constant<int, 8>{});
     else
-      launch_pdl(pdb::rope_kv_write_vec_kernel<float, kRows>, dim3(grid), dim3(256), smem, st, p);
+      go(std::integral_constant<int, 2>{});
   } else {
     const size_t smem = (size_t)p.dim * sizeof(float);
     if (dtype == PDB_DTYPE_FLOAT16)
@@ -714,7 +726,7 @@ int pdb_rope_kv_write(const void* q, const void* k, const void* v, void* q_out, 
       return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) +
                                          " bytes");
     int32_t* sor = static_cast<int32_t*>(workspace);
-    pdb::valid_scan_kernel<1024, 8><<<1, 1024, 0, st>>>(valid, rows, num_slots, sor);
+    pdb::valid_scan_kernel<1024, 16><<<1, 1024, 0, st>>>(valid, rows, num_slots, sor);
     slot_of_row = sor;
   }
   pdb::RopeParams p{};

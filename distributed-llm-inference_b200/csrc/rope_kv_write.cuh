@@ -37,11 +37,23 @@ valid_scan_kernel(const uint8_t* __restrict__ valid, int64_t rows,
   for (int64_t base = 0; base < rows; base += (int64_t)THREADS * ITEMS) {
     int flags[ITEMS];
     int local = 0;
+    const int64_t r_first = base + (int64_t)tid * ITEMS;
+    if (ITEMS == 16 && r_first + 16 <= rows &&
+        (reinterpret_cast<uintptr_t>(valid + r_first) & 15u) == 0) {  // one 16-byte load
+      const uint4 w = *reinterpret_cast<const uint4*>(valid + r_first);
+      const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      const int64_t r = base + (int64_t)tid * ITEMS + i;
-      flags[i] = (r < rows && valid[r]) ? 1 : 0;
-      local += flags[i];
+      for (int i = 0; i < ITEMS; ++i) {
+        flags[i] = ((wd[(i / 4) & 3] >> (8 * (i % 4))) & 0xffu) ? 1 : 0;
+        local += flags[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i) {
+        const int64_t r = r_first + i;
+        flags[i] = (r < rows && valid[r]) ? 1 : 0;
+        local += flags[i];
+      }
     }
     // inclusive warp scan of per-thread counts
     int incl = local;
