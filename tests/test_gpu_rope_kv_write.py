@@ -167,3 +167,38 @@ def test_rope_vector_and_scalar_paths(pkg, cuda, dtype, D):
     kv_cache.write_decode(exp_k, phys, off, ko.cpu()[:, 0])
     kv_cache.write_decode(exp_v, phys, off, v[:, 0])
     assert torch.equal(kd.cpu(), exp_k) and torch.equal(vd.cpu(), exp_v)
+
+
+@pytest.mark.parametrize("shared_positions", [True, False])
+def test_rope_many_short_rows(pkg, cuda, shared_positions):
+    """Many short rows (here 21 sequences x 120 positions, SmolLM2 heads: more
+    than 2048 rows of 72 16-byte work items) take the 8-rows-per-CTA launch;
+    with positions shared across sequences (a prefill batch) and with
+    sequences at different offsets, outputs match the oracle, the valid rows'
+    slots hold the rotated k and the input v, and nothing else is written."""
+    g = torch.Generator().manual_seed(31 if shared_positions else 32)
+    B, S, H, KVH, D, N, bs = 21, 120, 9, 3, 64, 200, 16
+    q = torch.randn(B, S, H, D, generator=g).half()
+    k = torch.randn(B, S, KVH, D, generator=g).half()
+    v = torch.randn(B, S, KVH, D, generator=g).half()
+    pos = torch.arange(S)[None, :].expand(B, -1).clone()
+    if not shared_positions:
+        pos = pos + torch.randint(0, 3000, (B, 1), generator=g)
+    lens = torch.randint(1, S + 1, (B,), generator=g)
+    valid = torch.arange(S)[None, :] < lens[:, None]
+    slots = torch.randperm(N * bs, generator=g)[: int(valid.sum())]
+    phys, offs = slots // bs, slots % bs
+    kp0 = torch.randn(N, bs, KVH, D, generator=g).half()
+    vp0 = torch.randn(N, bs, KVH, D, generator=g).half()
+    inv = W.inv_freq(1e5, D)
+    kd, vd = kp0.to(cuda), vp0.to(cuda)
+    qo, ko = pkg.rope_kv_write(q.to(cuda), k.to(cuda), v.to(cuda), kd, vd, phys.to(cuda),
+                               offs.to(cuda), pos.to(cuda), inv.to(cuda), valid=valid.to(cuda))
+    qr, kr = orope.rope(q, k, pos, inv, exact_trig=True)
+    assert_parity(qo, qr, "q")
+    assert_parity(ko, kr, "k")
+    exp_k, exp_v = kp0.clone(), vp0.clone()
+    kv_cache.write_prefill(exp_k, phys, offs, ko.cpu(), valid)
+    kv_cache.write_prefill(exp_v, phys, offs, v, valid)
+    assert torch.equal(kd.cpu(), exp_k) and torch.equal(vd.cpu(), exp_v)
+    assert pkg.read_device_errors() == 0
