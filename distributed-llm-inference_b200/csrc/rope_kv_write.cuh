@@ -76,11 +76,30 @@ valid_scan_kernel(const uint8_t* __restrict__ valid, int64_t rows,
     __syncthreads();
     const int carry = carry_s;
     int run = carry + (warp ? warp_sums[warp - 1] : 0) + incl - local;
+    if (ITEMS % 4 == 0 && r_first + ITEMS <= rows &&
+        (reinterpret_cast<uintptr_t>(slot_of_row + r_first) & 15u) == 0) {
+      // 16-byte stores: a thread's results are consecutive, so scalar
+      // stores would make every warp store instruction 32 partial sectors
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      const int64_t r = base + (int64_t)tid * ITEMS + i;
-      if (r < rows) slot_of_row[r] = flags[i] ? run : -1;
-      run += flags[i];
+      for (int i = 0; i < ITEMS; i += 4) {
+        int4 o;
+        o.x = flags[i] ? run : -1;
+        run += flags[i];
+        o.y = flags[i + 1] ? run : -1;
+        run += flags[i + 1];
+        o.z = flags[i + 2] ? run : -1;
+        run += flags[i + 2];
+        o.w = flags[i + 3] ? run : -1;
+        run += flags[i + 3];
+        *reinterpret_cast<int4*>(slot_of_row + r_first + i) = o;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i) {
+        const int64_t r = r_first + i;
+        if (r < rows) slot_of_row[r] = flags[i] ? run : -1;
+        run += flags[i];
+      }
     }
     __syncthreads();
     if (tid == THREADS - 1) carry_s = run;
