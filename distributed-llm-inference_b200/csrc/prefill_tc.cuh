@@ -167,6 +167,30 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed FP32 pairs (sm_100 f32x2 arithmetic: one instruction, two lanes).
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 __device__ __forceinline__ void tc_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
@@ -330,7 +354,6 @@ prefill_tc_kernel(const PrefillTcParams p, const __grid_constant__ CUtensorMap q
   int* lens = reinterpret_cast<int*>(items + IQ);  // [LCAP] clamped prompt lengths (producer)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t row_stride = (int64_t)p.H * D;
   if (tid == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
@@ -572,13 +595,17 @@ prefill_tc_kernel(const PrefillTcParams p, const __grid_constant__ CUtensorMap q
           for (int i = 0; i < BN; ++i)
             if (k0 + i >= lim) sc[i] = -INFINITY;
         }
-        float mx8[8];  // independent chains: the reductions are latency-, not issue-bound
+        static_assert(BN == 64, "the max and exponent loops below are written for 64 keys");
+        float mx8[8];  // independent chains of three-input max
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = sc[i];
-#pragma unroll
-        for (int i = 8; i < BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sc[i]);
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int i = 0; i < 8; ++i) {
+          mx8[i] = fmax3(sc[i], sc[i + 8], sc[i + 16]);
+          mx8[i] = fmax3(mx8[i], sc[i + 24], sc[i + 32]);
+          mx8[i] = fmax3(mx8[i], sc[i + 40], sc[i + 48]);
+          mx8[i] = fmaxf(mx8[i], sc[i + 56]);
+        }
+        const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                               fmaxf(mx8[6], mx8[7]));
         const float mt = mx * c;  // this tile's row max, log2 units
         float alpha = 1.f;
         if (mt > m_used + 8.f) {  // lazy rescale (always on the first tile)
@@ -586,16 +613,21 @@ prefill_tc_kernel(const PrefillTcParams p, const __grid_constant__ CUtensorMap q
           m_used = mt;
         }
         uint32_t pk[BN / 2];
-        float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const uint64_t c2 = f2(c, c), nm2 = f2(-m_used, -m_used);
+        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // row-sum pairs (0.f bits are 0)
 #pragma unroll
         for (int i = 0; i < BN / 2; ++i) {
-          const float a = ex2(fmaf(sc[2 * i], c, -m_used));
-          const float bb = ex2(fmaf(sc[2 * i + 1], c, -m_used));
-          rs8[i & 7] += a + bb;
+          float y0, y1;
+          f2_split(ffma2(f2(sc[2 * i], sc[2 * i + 1]), c2, nm2), y0, y1);
+          const float a = ex2(y0), bb = ex2(y1);
+          acc[i & 3] = fadd2(acc[i & 3], f2(a, bb));
           pk[i] = pack_half2(a, bb);
         }
+        float r8[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f2_split(acc[i], r8[2 * i], r8[2 * i + 1]);
         const float rs =
-            ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+            ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
         l = l * alpha + rs;
         // V rows of keys >= kend in the item's last tile: zero them (stale
         // pool bytes must not meet a zero P; 0 * NaN would poison the row)
