@@ -250,8 +250,11 @@ struct PrefillTc {
   static_assert(D <= 128 && S_COL + BN <= P_COL && P_COL + BN <= TMEM_COLS, "TMEM columns");
   static constexpr int NBARS = 2 * STAGES + QBUF + 6 + 2 * IQ;
   static constexpr int LCAP = 512;  // prompt lengths kept in shared memory (more: read from global)
+  // Output staging: per softmax warp 32 rows x 32 columns of FP16 (2 KB).
+  static constexpr int OUT_STAGE = 32 * 64;
   static constexpr size_t SMEM = 1024 + (size_t)QBUF * Q_BYTES + (size_t)STAGES * STAGE_BYTES +
-                                 NBARS * 8 + 16 + IQ * sizeof(PrefillItem) + LCAP * 4;
+                                 NBARS * 8 + 16 + IQ * sizeof(PrefillItem) + LCAP * 4 + 16 +
+                                 4 * OUT_STAGE;
 };
 
 // Walks the global item order: first every working tile, level by level
@@ -352,6 +355,8 @@ prefill_tc_kernel(const PrefillTcParams p, const __grid_constant__ CUtensorMap q
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + PT::NBARS);
   PrefillItem* items = reinterpret_cast<PrefillItem*>(tmem_slot + 4);
   int* lens = reinterpret_cast<int*>(items + IQ);  // [LCAP] clamped prompt lengths (producer)
+  unsigned char* out_stage = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(lens + PT::LCAP) + 15) & ~uintptr_t(15));  // [4][OUT_STAGE]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -673,27 +678,44 @@ prefill_tc_kernel(const PrefillTcParams p, const __grid_constant__ CUtensorMap q
       wait(&pv_done[(g - 1) & 1], (uint32_t)((g - 1) >> 1) & 1u);
       tc_fence_after();
       const float inv = 1.f / l;
+      // 32 columns at a time through this warp's staging buffer, so that
+      // one store instruction writes 8 rows x 64 contiguous bytes instead of
+      // 16 bytes of 32 rows (rows are H * D * 2 bytes apart). Row r's
+      // 16-byte chunk ch sits at r * 64 + ((ch ^ ((r >> 1) & 3)) << 4): the
+      // writes (a row per lane) and the reads (4 lanes per row) are both
+      // free of bank conflicts.
+      unsigned char* stg = out_stage + warp * PT::OUT_STAGE;
 #pragma unroll
       for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t ov[32];
         tc_ld32(tmem + lane_base + PT::O_COL + cc * 32, ov);
         tc_wait_ld();
         tc_reg_fence32(ov);
-        if (qr < n) {
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 o = make_uint4(0, 0, 0, 0);  // rows >= n: zeros
+          if (qr < n) {
             uint32_t wv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               wv[e] = pack_half2(__uint_as_float(ov[q4 * 8 + 2 * e]) * inv,
                                  __uint_as_float(ov[q4 * 8 + 2 * e + 1]) * inv);
-            *reinterpret_cast<uint4*>(orow + cc * 32 + q4 * 8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            o = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
-        } else if (qr < p.W) {
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            *reinterpret_cast<uint4*>(orow + cc * 32 + q4 * 8) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(stg + lane * 64 + ((q4 ^ ((lane >> 1) & 3)) << 4)) = o;
         }
+        __syncwarp();
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int r = k4 * 8 + (lane >> 2), ch = lane & 3;
+          const int row = it.t0 + warp * 32 + r;  // rows >= W belong to no prompt: not written
+          if (row < p.W) {
+            const uint4 o = *reinterpret_cast<const uint4*>(stg + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4));
+            *reinterpret_cast<uint4*>(p.out + (((int64_t)it.b * p.W + row) * p.H + it.hq) * D +
+                                      cc * 32 + ch * 8) = o;
+          }
+        }
+        __syncwarp();  // the buffer is rewritten for the next 32 columns
       }
       // The O reads are complete (tcgen05.wait::ld) before this warp's next
       // p_full arrival, which is what lets the next item's first PV overwrite O.
