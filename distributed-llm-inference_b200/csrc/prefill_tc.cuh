@@ -565,12 +565,14 @@ prefill_tc_kernel(const PrefillTcParams p, const __grid_constant__ CUtensorMap q
       const PrefillItem it = take_item(q);
       if (it.kind == kItemEnd) break;
       const int qr = it.t0 + tid;
-      __half* orow = p.out + (((int64_t)it.b * p.W + qr) * p.H + it.hq) * D;
-      if (it.kind != kItemWork) {  // rows >= n: zeros
-        if (qr < p.W) {
+      if (it.kind != kItemWork) {  // rows >= n: zeros, whole rows per warp store
 #pragma unroll
-          for (int cc = 0; cc < CH; ++cc)
-            reinterpret_cast<uint4*>(orow)[cc] = make_uint4(0, 0, 0, 0);
+        for (int k = 0; k < CH; ++k) {  // this warp's 32 rows x CH 16-byte chunks
+          const int qi = k * 32 + lane;
+          const int row = it.t0 + warp * 32 + qi / CH;
+          if (row < p.W)
+            reinterpret_cast<uint4*>(p.out + (((int64_t)it.b * p.W + row) * p.H + it.hq) * D)
+                [qi % CH] = make_uint4(0, 0, 0, 0);
         }
         continue;
       }
