@@ -31,9 +31,16 @@ def _check(cond: bool, msg: str) -> None:
 # Workspace cache: one grow-only buffer per (device, stream, op). Calls on one
 # stream are ordered, so calls of the same op can share it; the buffer never
 # needs clearing (counters carry a per-call tag, so stale bytes count as zero).
+# A CUDA graph captured with a call bakes in the buffer's address, and a
+# graph does not keep the tensor alive: a buffer that a larger call replaces
+# is therefore retired, never freed, so that graphs captured before the
+# growth (e.g. a decode tick of a smaller batch) keep valid scratch memory.
+# Buffers grow at least 2x at a time, so the retired ones together stay
+# smaller than the live one.
 # --------------------------------------------------------------------------
 _ws_lock = threading.Lock()
 _ws_cache: dict[tuple[int, int, str], torch.Tensor] = {}
+_ws_retired: list[torch.Tensor] = []
 
 
 def workspace(device: torch.device, stream: int, nbytes: int, tag: str) -> torch.Tensor | None:
@@ -44,7 +51,11 @@ def workspace(device: torch.device, stream: int, nbytes: int, tag: str) -> torch
     with _ws_lock:
         buf = _ws_cache.get(key)
         if buf is None or buf.numel() < nbytes:
-            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            size = max(nbytes, 1 << 20)
+            if buf is not None:
+                size = max(size, 2 * buf.numel())
+                _ws_retired.append(buf)
+            buf = torch.zeros(size, dtype=torch.uint8, device=device)
             _ws_cache[key] = buf
         return buf
 

@@ -147,7 +147,10 @@ PDB_API int pdb_paged_attention_impl(const void* q, const void* k_pool,
  *     Llama-3-8B shape at batch 256 the need is about 1.3 MB.
  *   - The first call on a device looks up that device's copy of the array
  *     (the device must be current); make that first call before any stream
- *     capture on the device.
+ *     capture on the device. The address is kept for the life of the
+ *     process: after cudaDeviceReset (or anything else that destroys the
+ *     device's primary context) this entry point must not be called again
+ *     in that process.
  *   - Every call on a device shares the one array: calls whose kernels can
  *     overlap on the GPU (different streams without ordering) race and give
  *     wrong results. Each call clears the part that must start at zero.

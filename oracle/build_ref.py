@@ -10,6 +10,9 @@ the GPU box with the working tree, where tests and the bench load it with
 load_ref_module() to check parity against and time the reference kernel.
 
     python oracle/build_ref.py [/path/to/reference]
+
+Without an argument the checkout is found by oracle/refroot.py
+(PDB_REFERENCE_ROOT, else a ``reference`` directory beside this repository).
 """
 from __future__ import annotations
 
@@ -22,7 +25,6 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 NAME = "ref_paged_attention"
-DEFAULT_REF = Path("/root/reference")
 
 
 def built_path() -> Path | None:
@@ -30,7 +32,12 @@ def built_path() -> Path | None:
     return hits[0] if hits else None
 
 
-def build(ref_root: Path = DEFAULT_REF, verbose: bool = False) -> Path | None:
+def build(ref_root: Path | None = None, verbose: bool = False) -> Path | None:
+    if ref_root is None:
+        from oracle.refroot import reference_root
+        ref_root = reference_root()
+    if ref_root is None:
+        return built_path()
     src = [ref_root / "cuda" / "binding.cpp", ref_root / "cuda" / "paged_attention.cu"]
     if not all(p.exists() for p in src):
         return built_path()
@@ -59,4 +66,5 @@ def load_ref_module():
 
 
 if __name__ == "__main__":
-    print(build(Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REF, verbose=True))
+    sys.path.insert(0, str(HERE.parent))
+    print(build(Path(sys.argv[1]) if len(sys.argv) > 1 else None, verbose=True))

@@ -70,12 +70,15 @@ def paged_attention_fp64(query, keys, values, tables, lengths) -> torch.Tensor:
     return out
 
 
-def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      native: bool = False) -> torch.Tensor:
     """worker/llama.py:141-144: causal SDPA over the padded prompt batch,
     K/V repeated per query group. q [B, W, H, D], k/v [B, W, KVH, D];
-    returns [B, W, H, D] (computed in fp32)."""
+    returns [B, W, H, D]. Computed in fp32 (the precision the reference's
+    FP16 CUDA SDPA accumulates in), or with ``native`` in the inputs' dtype,
+    which on the CPU is the reference's own call bit for bit."""
     groups = q.shape[2] // k.shape[2]
-    qf, kf, vf = q.float(), k.float(), v.float()
+    qf, kf, vf = (q, k, v) if native else (q.float(), k.float(), v.float())
     ctx = F.scaled_dot_product_attention(
         qf.transpose(1, 2), kf.repeat_interleave(groups, dim=2).transpose(1, 2),
         vf.repeat_interleave(groups, dim=2).transpose(1, 2), is_causal=True)

@@ -1,9 +1,11 @@
 """Generate the golden fixtures of tests/golden/ from the REFERENCE's own code.
 
-Run in a container that has the reference checkout (read-only) at
-/root/reference:
+Run where the reference checkout (read-only) is available:
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [/path/to/reference]
+
+Without an argument the checkout is found by oracle/refroot.py
+(PDB_REFERENCE_ROOT, else a ``reference`` directory beside this repository).
 
 It imports worker.llama (torch_paged_attention, PagedLlama.rope) and
 worker.engine (PagedKV) from the reference, feeds them the seeded inputs of
@@ -105,6 +107,97 @@ def rope_inputs(spec):
     k = (torch.randn(1, P, spec["KVH"], spec["D"], generator=g) * 3).to(dtype)
     pos = torch.tensor([ROPE_POSITIONS], dtype=torch.int64)
     return q, k, pos
+
+
+PREFILL_ATTENTION = dict(
+    model_seed=4321, token_seed=8, blocks=40, block_size=16,
+    # earlier requests whose pages are released uncleared before the prompts
+    # are admitted, so the prompts' pages are fragmented and hold stale rows
+    warm={"w0": 50, "w1": 33, "w2": 90},
+    # ragged prompts: partial pages, exact page multiples, a single token
+    prompts={"p0": 37, "p1": 5, "p2": 64, "p3": 70, "p4": 16, "p5": 1},
+)
+
+
+def prefill_attention_config():
+    """The tiny Llama of the runner fixtures (GQA 2, head_dim 64) with weights
+    drawn at std 0.05, so that q, k and v come out near unit scale and the
+    attention outputs are large enough for an absolute FP16 bar to mean
+    something (at the default std 0.02 they would be ~1e-2)."""
+    from oracle import llama_model as LM
+    cfg = LM.tiny_llama_config()
+    cfg.initializer_range = 0.05
+    return cfg
+
+
+def prefill_attention_capture(paged_llama_cls, dtype_name: str) -> dict:
+    """Run the reference's PagedLlama.prefill on the spec above and record,
+    per layer, what its attention consumed and produced: the rotated q (the
+    output of its rope call), the k/v rows it wrote to the pool (read back
+    from the cache through the slots), and the attention context (the input
+    of o_proj). Only rows of real prompt tokens are kept; padded rows feed no
+    real token's output."""
+    from oracle import llama_model as LM
+    spec = PREFILL_ATTENTION
+    dtype = getattr(torch, dtype_name)
+    cfg = prefill_attention_config()
+    model = LM.seeded_model(cfg, seed=spec["model_seed"], dtype=dtype)
+    cfg.rope_theta = LM.rope_theta(cfg)   # transformers-5 shim, as in section 7
+    cfg.rope_scaling = None
+    runner = paged_llama_cls(model, None, blocks=spec["blocks"],
+                             block_size=spec["block_size"], attention="torch")
+    g = torch.Generator().manual_seed(spec["token_seed"])
+
+    def toks(n):
+        return torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist()
+
+    warm = spec["warm"]
+    for rid, n in warm.items():
+        assert runner.cache.reserve(rid, n)
+    runner.prefill(list(warm), [toks(n) for n in warm.values()])
+    for rid in ("w1", "w0", "w2"):
+        runner.cache.release(rid)
+    prompts = spec["prompts"]
+    for rid, n in prompts.items():
+        assert runner.cache.reserve(rid, n)
+    ids = list(prompts)
+    token_lists = [toks(n) for n in prompts.values()]
+
+    layers = len(model.model.layers)
+    qs, ctxs = [None] * layers, [None] * layers
+    calls = []
+
+    def rope_hook(q, k, positions):
+        qo, ko = paged_llama_cls.rope(runner, q, k, positions)
+        qs[len(calls)] = qo.clone()
+        calls.append(1)
+        return qo, ko
+
+    runner.rope = rope_hook
+    hooks = [layer.self_attn.o_proj.register_forward_pre_hook(
+        lambda mod, args, i=i: ctxs.__setitem__(i, args[0].clone()))
+        for i, layer in enumerate(model.model.layers)]
+    try:
+        runner.prefill(ids, token_lists)
+    finally:
+        for h in hooks:
+            h.remove()
+        del runner.rope
+    tables, lengths, _ = runner.cache.metadata(ids)
+    lens = list(prompts.values())
+    width = max(lens)
+    valid = torch.arange(width)[None, :] < torch.tensor(lens)[:, None]
+    physical, offsets = runner.cache.slots(ids, [range(n) for n in lens])
+    H, KVH, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    out = dict(spec=spec, dtype=dtype_name, heads=H, kv_heads=KVH, head_dim=D,
+               tables=tables, lengths=lengths, layers=[])
+    for i in range(layers):
+        out["layers"].append(dict(
+            q=qs[i][valid],                                              # [T, H, D]
+            k=runner.cache.keys[i][physical, offsets].clone(),           # [T, KVH, D]
+            v=runner.cache.values[i][physical, offsets].clone(),
+            context=ctxs[i].view(len(ids), width, H, D)[valid]))         # [T, H, D]
+    return out
 
 
 def main(ref_root: str) -> None:
@@ -209,8 +302,17 @@ def main(ref_root: str) -> None:
                     k_pool_digest=digest(runner.cache.keys),
                     v_pool_digest=digest(runner.cache.values)),
                HERE / "llama_tiny_scenario.pt")
+    # 8. Prefill attention of the reference's own PagedLlama.prefill
+    #    (worker/llama.py:141-144: causal SDPA over the padded prompt batch,
+    #    K/V repeated per query group), FP32 and FP16, on the CPU.
+    torch.save({dtype: prefill_attention_capture(PagedLlama, dtype)
+                for dtype in ("float32", "float16")}, HERE / "prefill_attention.pt")
     print("wrote", sorted(p.name for p in HERE.glob("*.pt")))
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    from oracle.refroot import reference_root
+    root = sys.argv[1] if len(sys.argv) > 1 else reference_root()
+    if root is None:
+        sys.exit("reference checkout not found: pass its path or set PDB_REFERENCE_ROOT")
+    main(str(root))

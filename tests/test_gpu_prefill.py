@@ -14,8 +14,8 @@ from __future__ import annotations
 import pytest
 import torch
 
-from conftest import import_module
-from gpu_helpers import assert_parity
+from conftest import REPO, import_module
+from gpu_helpers import assert_parity, prefill_fixture_layer, prefill_fixture_pools
 from oracle import kv_cache
 from oracle import paged_attention as opa
 
@@ -24,6 +24,26 @@ W = import_module("workloads")
 
 
 IMPLS = pytest.mark.parametrize("impl", ["tcgen05", "mma"])
+
+
+@IMPLS
+def test_prefill_attention_matches_reference_fixture(pkg, cuda, impl):
+    """Both kernels against the reference's own output: the FP16 contexts
+    that PagedLlama.prefill (worker/llama.py:141-144) computed on a seeded
+    tiny Llama (tests/golden/prefill_attention.pt), fed the same rotated q and
+    the same k/v rows, placed at the reference's slots in pools whose every
+    other row is NaN. Every real token's row within 2e-3; padded rows zero."""
+    case = torch.load(REPO / "tests" / "golden" / "prefill_attention.pt",
+                      weights_only=False)["float16"]
+    tables, lengths = case["tables"].to(cuda), case["lengths"].to(cuda)
+    for layer in range(len(case["layers"])):
+        q, _, _, ctx, valid = prefill_fixture_layer(case, layer)
+        k_pool, v_pool = prefill_fixture_pools(case, layer)
+        out = pkg.prefill_attention(q.to(cuda), k_pool.to(cuda), v_pool.to(cuda), tables,
+                                    lengths, impl=_impl(pkg, impl)).cpu()
+        assert_parity(out[valid], ctx[valid], f"reference prefill fixture, {impl}, layer {layer}")
+        assert torch.equal(out[~valid], torch.zeros_like(out[~valid]))
+    assert pkg.read_device_errors() == 0
 
 
 def _impl(pkg, name):

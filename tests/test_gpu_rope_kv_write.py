@@ -114,10 +114,30 @@ def test_prefill_write(pkg, cuda):
     touched = torch.zeros(pw.num_blocks, dtype=torch.bool)
     touched[d["physical"].unique()] = True
     assert torch.equal(dd["k_pool"].cpu()[~touched], d["k_pool"][~touched])
-    # byte-identical to the reference whenever its cos/sin agree with ours
-    same = mg.digest(dd["k_pool"]) == g["k_pool_digest"]
-    print(f"prefill pool digest equal to the reference: {same}; "
-          f"k exact fraction {exact_fraction(ko, kr):.6f}")
+    # Against the reference's own pools (digests of tests/golden/prefill.pt).
+    # v rows are copies: the v pool is byte-identical to the reference's.
+    assert mg.digest(dd["v_pool"]) == g["v_pool_digest"]
+    # The reference's k pool, restated on the CPU with its fp32 cos/sin
+    # calls (the oracle's default path reproduces its digest).
+    _, kr_ref = orope.rope(d["q"], d["k"], d["positions"], d["inv_freq"])
+    ref_k = d["k_pool"].clone()
+    kv_cache.write_prefill(ref_k, d["physical"], d["offsets"], kr_ref, d["valid"])
+    assert mg.digest(ref_k) == g["k_pool_digest"]
+    # The kernel's k pool equals the reference's wherever the reference's
+    # fp32 cos/sin round to the correctly rounded FP16 values; where they do
+    # not (a handful of angles, host dependent), it holds the correctly
+    # rounded result instead.
+    trig_differs = torch.zeros_like(ref_k, dtype=torch.bool)
+    kv_cache.write_prefill(trig_differs, d["physical"], d["offsets"], kr_ref != kr, d["valid"])
+    exact_k = d["k_pool"].clone()
+    kv_cache.write_prefill(exact_k, d["physical"], d["offsets"], kr, d["valid"])
+    got = dd["k_pool"].cpu()
+    mismatch = got != ref_k
+    unexplained = int((mismatch & ~trig_differs).sum())
+    assert unexplained == 0, (f"{unexplained} k-pool elements differ from the reference "
+                              f"where its cos/sin are correctly rounded")
+    assert torch.equal(got[trig_differs], exact_k[trig_differs])
+    assert int(trig_differs.sum()) <= 64, int(trig_differs.sum())
     assert pkg.read_device_errors() == 0
 
 

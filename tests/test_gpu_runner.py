@@ -146,6 +146,40 @@ def test_graph_ticks_equal_eager_ticks(pkg, cuda):
     assert pkg.read_device_errors() == 0
 
 
+def test_graphs_of_two_batch_sizes_keep_their_workspaces(pkg, cuda):
+    """A tick graph captured at batch 1 keeps valid attention scratch after a
+    batch-8 tick grows the stream's workspace (the graph addresses the buffer
+    it was captured with; that buffer must not return to the allocator):
+    later replays of the batch-1 graph match eager ticks bit for bit, and
+    tensors allocated after the growth keep their contents."""
+    eager = _fresh_runner(torch.float16, 64, 16)
+    graphed = _fresh_runner(torch.float16, 64, 16, graphs=True)
+    gen = torch.Generator().manual_seed(5)
+    ids = [f"r{i}" for i in range(8)]
+    prompts = [torch.randint(0, 512, (int(n),), generator=gen).tolist()
+               for n in torch.randint(3, 60, (8,), generator=gen)]
+    plan = [ids[:1]] * 3 + [ids] * 3 + [ids[:1]] * 3
+    tokens = [torch.randint(0, 512, (len(b),), generator=gen).tolist() for b in plan]
+    for run in (eager, graphed):
+        for r in ids:
+            assert run.cache.reserve(r, 100)
+        run.prefill(ids, prompts)
+    ws = import_module("ops")._ws_cache
+    fill = []
+    for step, (batch, toks) in enumerate(zip(plan, tokens)):
+        if step == 6:  # the batch-8 ticks have grown the workspace: reuse freed memory now
+            fill = [torch.full((1 << 18,), 1234567, dtype=torch.int32, device=cuda)
+                    for _ in range(24)]
+        a = eager.decode(batch, toks)
+        b = graphed.decode(batch, toks)
+        assert torch.equal(a, b), f"step {step}, batch {len(batch)}"
+    assert sorted(graphed._b200_graphs) == [1, 8]
+    assert all(bool((t == 1234567).all()) for t in fill)
+    assert torch.equal(eager.cache.keys, graphed.cache.keys)
+    assert len(ws) > 0
+    assert pkg.read_device_errors() == 0
+
+
 def test_install_on_a_llama_module(pkg, cuda):
     """install() routes PagedLlama.decode/prefill of a worker.llama-shaped
     module to the B200 methods for attention='cuda' instances (their own

@@ -14,6 +14,7 @@ import pytest
 import torch
 
 from conftest import REPO, golden_module, import_module
+from gpu_helpers import prefill_fixture_layer
 from oracle import kv_cache, paged_attention as opa, rope as orope, scalar
 
 mg = golden_module()
@@ -145,3 +146,38 @@ def test_allocator_restatement():
     assert c.free[-1] == 3 and float(c.keys[0, 3].sum()) != 0.0   # not cleared
     with pytest.raises(ValueError):
         c.reserve("a", 1)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16"])
+def test_prefill_attention_fixture(dtype):
+    """The reference's PagedLlama.prefill attention (worker/llama.py:141-144)
+    on a seeded tiny Llama: ragged prompts on fragmented, reused pages. The
+    oracle's call in the inputs' dtype is the reference's bit for bit; its
+    fp32 form (what the GPU kernels are held to) is within one FP16 ulp of
+    the FP16 reference and equal to the FP32 one."""
+    case = load("prefill_attention.pt")[dtype]
+    assert case["dtype"] == dtype and case["spec"] == mg.PREFILL_ATTENTION
+    for layer in range(len(case["layers"])):
+        q, k, v, ctx, valid = prefill_fixture_layer(case, layer)
+        native = opa.prefill_attention(q, k, v, native=True)
+        assert native.dtype == q.dtype
+        assert torch.equal(native[valid], ctx[valid]), f"layer {layer}"
+        f32 = opa.prefill_attention(q, k, v)
+        if dtype == "float32":
+            assert torch.equal(f32[valid], ctx[valid])
+        else:
+            err = (f32[valid].half().float() - ctx[valid].float()).abs()
+            assert err.max().item() <= 1e-3, f"layer {layer}: {err.max().item()}"
+
+
+def test_prefill_attention_fixture_layout():
+    """Pages of the fixture's prompts are fragmented and reused (the earlier
+    requests' rows were released uncleared), and the prompts cross pages."""
+    case = load("prefill_attention.pt")["float16"]
+    lens = case["lengths"].tolist()
+    bs = case["spec"]["block_size"]
+    assert lens == list(case["spec"]["prompts"].values())
+    assert any(n % bs for n in lens) and any(n % bs == 0 for n in lens) and 1 in lens
+    used = [int(p) for b, n in enumerate(lens) for p in case["tables"][b, :(n + bs - 1) // bs]]
+    assert len(set(used)) == len(used)
+    assert any(b - a != 1 for a, b in zip(used, used[1:]))

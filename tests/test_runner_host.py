@@ -14,9 +14,10 @@ import torch
 from conftest import REPO, golden_module, import_module, import_pkg
 from oracle import kv_cache
 from oracle import llama_model as LM
+from oracle.refroot import reference_root
 
 P = import_module("paged_kv")
-REF = Path("/root/reference")
+REF = reference_root() or Path("reference-checkout-not-found")
 
 
 def gold():
