@@ -65,8 +65,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16", "smollm_tick", "prefill",
-                                           "prefill_write"],
+    ap.add_argument("--workload", choices=["llama3_8b", "smollm_fp16", "smollm_fp32",
+                                           "smollm_tick", "prefill", "prefill_write"],
                     default="llama3_8b")
     ap.add_argument("--batch", type=int, default=None, help="override the workload batch")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling)")
@@ -78,13 +78,41 @@ def parse():
                     help="pin the prefill attention kernel (prefill workload)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the other configurations' measurements (the `secondary` object)")
     return ap.parse_args()
 
 
 def make_workload(args):
     if args.workload == "llama3_8b":
         return W.llama3_8b(batch=args.batch or 256, layers=args.layers or 32)
+    if args.workload == "smollm_fp32":
+        return W.smollm_fp32(batch=args.batch or 64, layers=args.layers or 30)
     return W.smollm_fp16(batch=args.batch or 64, layers=args.layers or 30)
+
+
+def decode_config(full, args, world: int) -> dict:
+    """The headline line's config, identical in both arms: the workload, the
+    sharding of its sequences over `world` ranks and the L2 note."""
+    ranks = [full.shard(r, world, args.sharding) for r in range(world)] if world > 1 else [full]
+    w0 = ranks[0]
+    return {
+        "workload": (f"{full.name}: batch {full.batch}, {full.heads}/{full.kv_heads} heads, "
+                     f"head_dim {full.head_dim}, {full.layers} layers, block {full.block_size}, "
+                     "lengths lognormal(1024, 0.8) in [16, 8192]"
+                     if args.workload == "llama3_8b" else full.name),
+        "batch": full.batch, "layers": full.layers, "max_length": full.max_length,
+        "mean_length": float(full.lengths.float().mean()),
+        "sharding": (f"{args.sharding}: every rank owns B/P whole sequences and its own "
+                     "pools/tables" + ("; balanced = dealt longest-first to the rank with "
+                                       "the fewest KV tokens" if args.sharding == "balanced"
+                                       else "; contiguous = sequences [r*B/P, (r+1)*B/P)")),
+        "max_rank_tokens": max(float(r.lengths.sum()) for r in ranks),
+        "mean_rank_tokens": float(full.lengths.sum()) / world,
+        "l2": "inputs larger than L2 (KV pools %.1f GB per rank)" % (
+            2 * w0.layers * w0.num_blocks * w0.block_size * w0.kv_heads * w0.head_dim
+            * w0.elem_bytes / 1e9),
+    }
 
 
 # --------------------------------------------------------------------------
@@ -505,52 +533,47 @@ def run_ours(args):
         import torch.distributed as dist
         dist.all_reduce(chk)
 
-    max_rank_tokens = max_over_ranks(float(w.lengths.sum()), world, device)
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = cpu_baseline(w, t)
+
+    # the other configurations, after the headline workload's memory is freed
+    step_fused, n_layers = step.fused, w.layers
+    out_checksum = float(chk.item())
+    secondary = None
+    if not args.no_secondary and args.workload == "llama3_8b":
+        del step, t, g_step, g_attn, g_pro, g_two
+        torch.cuda.synchronize(device)
+        torch.cuda.empty_cache()
+        secondary = secondary_ours(args, device, world)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": full.batch / (ms_step * 1e-3), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f16", "data": "synthetic (seeded; no dataset in this path)",
-            "config": {
-                "workload": f"{full.name}: batch {full.batch}, {full.heads}/{full.kv_heads} heads, "
-                            f"head_dim {full.head_dim}, {full.layers} layers, block {full.block_size}, "
-                            f"lengths lognormal(1024, 0.8) in [16, 8192]"
-                            if args.workload == "llama3_8b" else full.name,
-                "batch": full.batch, "layers": full.layers, "max_length": full.max_length,
-                "mean_length": float(full.lengths.float().mean()),
-                "sharding": (f"{args.sharding}: every rank owns B/P whole sequences and its own "
-                             "pools/tables" + ("; balanced = dealt longest-first to the rank with "
-                                               "the fewest KV tokens" if args.sharding == "balanced"
-                                               else "; contiguous = sequences [r*B/P, (r+1)*B/P)")),
-                "max_rank_tokens": max_rank_tokens,
-                "mean_rank_tokens": float(full.lengths.sum()) / world,
-                "l2": "inputs larger than L2 (KV pools %.1f GB per rank)" % (
-                    2 * w.layers * w.num_blocks * w.block_size * w.kv_heads * w.head_dim
-                    * w.elem_bytes / 1e9),
-                "step": ("per layer: decode_attention (RoPE + KV-slot write + attention in one "
-                         "launch), one CUDA graph per step" if step.fused else
-                         "per layer: rope_kv_write + paged_attention, one CUDA graph per step"),
-            },
+            "dtype": "f16" if full.dtype == torch.float16 else "f32",
+            "data": "synthetic (seeded; no dataset in this path)",
+            "config": decode_config(full, args, world),
+            "step": ("per layer: decode_attention (RoPE + KV-slot write + attention in one "
+                     "launch), one CUDA graph per step" if step_fused else
+                     "per layer: rope_kv_write + paged_attention, one CUDA graph per step"),
             "algorithmic_gb_per_step": full.seq_step_bytes() / 1e9,
             "achieved_gbs_step": full.seq_step_bytes() / (ms_step * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": attn_kernel_label(w.head_dim, step.fused),
+                         "kernel": attn_kernel_label(w.head_dim, step_fused, w.dtype),
                          "peak_source": f"{peak_src} hbm_gbs",
                          "algorithmic_bytes_per_launch": attn_bytes,
                          "ms_per_launch": ms_attn, "prologue_ms_per_launch": ms_pro,
                          "two_launch_ms_per_step": ms_two},
             "clocks": clk,
-            "gpu_launches": args.steps * w.layers * (1 if step.fused else 2),
+            "gpu_launches": args.steps * n_layers * (1 if step_fused else 2),
             "e2e": e2e,
             "cpu_baseline": base,
             "alt_sharding": alt,
-            "checksum": float(chk.item()),
+            "checksum": out_checksum,
+            "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
     g_step = g_attn = g_pro = None
@@ -562,8 +585,11 @@ def run_ours(args):
 
 # The kernel a decode layer launches for an FP16 workload with GQA group <= 4
 # (head_dim 128: 64-token tiles; head_dim 64: 128-token tiles, two 16-token
-# blocks per warp).
-def attn_kernel_label(head_dim: int, fused: bool) -> str:
+# blocks per warp), or the FP32 SIMT kernel.
+def attn_kernel_label(head_dim: int, fused: bool, dtype: torch.dtype = torch.float16) -> str:
+    if dtype == torch.float32:
+        return (f"attn_streamk_kernel<SimtMath<float,{head_dim},4>>: FP32 SIMT stream-K "
+                "(fp32 FMA throughout), cp.async-staged K/V, split pieces merged in-kernel")
     m = "MmaMath<128,4,3,TMA>" if head_dim == 128 else f"MmaMath<{head_dim},4,3,TMA,2>"
     if fused:
         return (f"attn_tma_dyn_kernel<{m}, fused prologue>: RoPE + KV-slot write + attention, "
@@ -572,12 +598,166 @@ def attn_kernel_label(head_dim: int, fused: bool) -> str:
             "tail, epilogue warp")
 
 
+# --------------------------------------------------------------------------
+# measurements shared by the headline line, its `secondary` object and the
+# stand-alone --workload runs
+# --------------------------------------------------------------------------
+def _peaks() -> dict:
+    pk = REPO / "MEASURED_PEAKS.json"
+    return json.loads(pk.read_text()) if pk.exists() else {}
+
+
+def _roofline(achieved: float, bound: str, kernel: str, **extra) -> dict:
+    """Roofline entry against the measured peaks (burst figures: every kernel
+    here is timed in launches of tens of microseconds to milliseconds)."""
+    pk = _peaks()
+    if bound == "hbm":
+        peak, unit = pk.get("hbm_gbs"), "GB/s"
+        src = "measured hbm_gbs" if peak else "fallback 6.65 TB/s"
+        peak = peak or 6650.0
+    else:
+        peak, unit = pk.get("bf16_tflops"), "TFLOP/s"
+        src = "measured bf16_tflops (burst)" if peak else "fallback 1.59 PFLOP/s"
+        peak = peak or 1590.0
+    return {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": achieved / peak, "traffic": None, "kernel": kernel, "peak_source": src,
+            **extra}
+
+
+def timed_replays(run, stream, device, units: int, min_s: float = 0.3, max_reps: int = 200):
+    """Median ms per unit over back-to-back timed replays of `run` (each
+    replay does `units` units of work, bracketed by CUDA events on `stream`),
+    repeated until `min_s` seconds have passed so that the clock sampler sees
+    the timed region; clocks are sampled throughout."""
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    times, t_end = [], time.perf_counter() + min_s
+    while (time.perf_counter() < t_end and len(times) < max_reps) or len(times) < 3:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            s.record(stream)
+            run()
+            e.record(stream)
+        e.synchronize()
+        times.append(s.elapsed_time(e) / units)
+    return statistics.median(times), clocks.stop(), len(times)
+
+
+def measure_decode(w, device, steps: int, warmup: int) -> dict:
+    """Decode steps of workload `w` (every layer: RoPE + KV-slot write +
+    attention) through the public ops, one CUDA graph per step, K steps per
+    timed replay; the step's attention launches replayed alone give the
+    roofline figure. Inputs are larger than L2 (all layers' pools)."""
+    t = W.materialize(w, device)
+    step = DecodeStep(w, t)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize(device)
+    g_step = capture(step, stream)
+    g_dom = g_step if step.fused else capture(
+        lambda: [step.attention(i) for i in range(w.layers)], stream)
+    for _ in range(warmup):
+        with torch.cuda.stream(stream):
+            g_step.replay()
+    torch.cuda.synchronize(device)
+
+    def k_steps():
+        for _ in range(steps):
+            g_step.replay()
+    ms, clk, reps = timed_replays(k_steps, stream, device, steps)
+    ms_launch, _, _ = timed_replays(g_dom.replay, stream, device, w.layers, min_s=0.05)
+    nbytes = w.fused_bytes() if step.fused else w.attention_bytes()
+    kernel = attn_kernel_label(w.head_dim, step.fused, w.dtype)
+    pools_gb = 2 * w.layers * w.num_blocks * w.block_size * w.kv_heads * w.head_dim \
+        * w.elem_bytes / 1e9
+    res = {"metric": METRIC, "value": w.batch / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
+           "ms_per_launch": ms_launch, "dtype": "f16" if w.dtype == torch.float16 else "f32",
+           "config": {"workload": f"{w.name}: batch {w.batch}, {w.heads}/{w.kv_heads} heads, "
+                                  f"head_dim {w.head_dim}, {w.layers} layers, block "
+                                  f"{w.block_size}", "batch": w.batch, "layers": w.layers,
+                      "max_length": w.max_length,
+                      "mean_length": float(w.lengths.float().mean()),
+                      "l2": "inputs larger than L2 (KV pools %.1f GB)" % pools_gb},
+           "step": ("per layer: decode_attention (one launch)" if step.fused else
+                    "per layer: rope_kv_write + paged_attention (two launches)"),
+           "timing": f"median of {reps} CUDA-event-timed replays of {steps} graph steps",
+           "roofline": _roofline(nbytes / (ms_launch * 1e-3) / 1e9, "hbm", kernel,
+                                 algorithmic_bytes_per_launch=nbytes, ms_per_launch=ms_launch),
+           "clocks": clk, "gpu_launches": steps * w.layers * (1 if step.fused else 2)}
+    del g_step, g_dom, step, t
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_decode_reference(w, device, steps: int, mod) -> dict:
+    """The reference's decode attention on this GPU for workload `w`, as its
+    PagedLlama.decode runs it per layer: RoPE in torch ops
+    (worker/llama.py:108-117), the two slot writes (:171-172) and its own CUDA
+    kernel (cuda/paged_attention.cu:10-74, built from the reference's sources
+    into oracle/_ref), launched eagerly as the reference launches them. The
+    kernel alone is timed too (one launch per layer on the same pools)."""
+    from oracle import kv_cache, rope as orope
+    t = W.materialize(w, device)
+    pos, phys, off = t.positions, t.physical, t.offsets
+
+    def attention(layer, q):
+        return mod.paged_attention(q.contiguous(), t.k_pools[layer], t.v_pools[layer],
+                                   t.tables, t.lengths, w.max_length)
+
+    def step():
+        for layer in range(w.layers):
+            qr, kr = orope.rope(t.q[layer].unsqueeze(1), t.k[layer].unsqueeze(1), pos,
+                                t.inv_freq)
+            kv_cache.write_decode(t.k_pools[layer], phys, off, kr[:, 0])
+            kv_cache.write_decode(t.v_pools[layer], phys, off, t.v[layer])
+            attention(layer, qr[:, 0])
+
+    def kernels():
+        for layer in range(w.layers):
+            attention(layer, t.q[layer])
+    stream = torch.cuda.current_stream(device)
+    step()
+    torch.cuda.synchronize(device)
+    ms, clk, reps = timed_replays(step, stream, device, 1, min_s=0.3, max_reps=max(steps, 3))
+    ms_launch, _, _ = timed_replays(kernels, stream, device, w.layers, min_s=0.1,
+                                    max_reps=max(steps, 3))
+    nbytes = w.attention_bytes()
+    res = {"metric": METRIC, "value": w.batch / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
+           "ms_per_launch": ms_launch, "config": {"workload": w.name, "batch": w.batch,
+                                                  "layers": w.layers},
+           "step": "per layer: PagedLlama.rope (torch ops), two index_put slot writes, the "
+                   "reference's CUDA kernel; eager launches",
+           "timing": f"median of {reps} CUDA-event-timed steps",
+           "roofline": _roofline(nbytes / (ms_launch * 1e-3) / 1e9, "hbm",
+                                 "reference attention_kernel (cuda/paged_attention.cu), one CTA "
+                                 "per (sequence, head)", algorithmic_bytes_per_launch=nbytes),
+           "clocks": clk}
+    del t
+    torch.cuda.empty_cache()
+    return res
+
+
+def _reference_kernel_module():
+    """The reference's own CUDA kernel, prebuilt into oracle/_ref (None when
+    it was not built)."""
+    from oracle import build_ref
+    return build_ref.load_ref_module()
+
+
+# --------------------------------------------------------------------------
+# the reference arm: the reference's own CPU path, timed on the host cores
+# --------------------------------------------------------------------------
 def run_reference(args):
     """The reference's own CPU implementation of the path (oracle port of
-    worker/llama.py:58-71, :108-117, :171-172; the reference compiles no
-    CPU code) on the host cores, same workload/metric. Each step is a
-    bounded sample: 4 sequences of one layer, scaled to seq-steps/s."""
-    world, rank, _ = dist_env()
+    worker/llama.py:58-71, :108-117, :171-172; the reference compiles no CPU
+    code) on the host cores, same workload, metric and config. One step is a
+    bounded sample: 4 sequences through one layer, the same for every layer
+    (all layers have identical shapes and lengths), so seq-steps/s =
+    4 / (step time x layers). At N = 1 the line also carries the reference's
+    own GPU code timed on this box (its CUDA kernel and torch paths) for the
+    headline and the other configurations."""
+    world, rank, local = dist_env()
     if rank != 0:
         return
     from oracle import kv_cache, paged_attention as opa, rope as orope
@@ -604,19 +784,33 @@ def run_reference(args):
                             full.max_length)
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
-    sec = sum(times) / len(times) * full.layers  # one step of the sample, all layers
-    value = n / sec
+    sec = sum(times) / len(times)  # one sample step: n sequences through one layer
+    value = n / (sec * full.layers)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3 * full.batch / n,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic (seeded)", "impl": "reference",
-            "config": {"workload": full.name, "batch": full.batch, "layers": full.layers,
-                       "max_length": full.max_length},
+            "data": "synthetic (seeded; no dataset in this path)", "impl": "reference",
+            "config": decode_config(full, args, world),
+            "step": f"a bounded sample: {n} of {full.batch} sequences through one layer "
+                    "(RoPE, slot writes, gather + repeat + masked SDPA), padded to the "
+                    f"batch's max_length {full.max_length}",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
                              "kind": "port",
-                             "sample": f"{n} of {full.batch} sequences x 1 layer per step, scaled by "
-                                       f"{full.layers} layers; padded to max_length {full.max_length}"},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                             "sample": f"{n} of {full.batch} sequences x 1 layer per step, "
+                                       f"scaled by {full.layers} layers; padded to max_length "
+                                       f"{full.max_length}; os.cpu_count()={os.cpu_count()}"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    if world == 1 and torch.cuda.is_available() and not args.no_secondary:
+        device = torch.device("cuda", local)
+        torch.cuda.set_device(device)
+        mod = _reference_kernel_module()
+        if mod is None:
+            line["reference_cuda"] = {"unavailable": "the reference kernel was not built "
+                                                     "into oracle/_ref"}
+        else:
+            line["reference_cuda"] = measure_decode_reference(full, device, 3, mod)
+        line["secondary"] = secondary_reference(args, device, mod)
     print(json.dumps(line), flush=True)
 
 
@@ -628,24 +822,24 @@ TICK_UNIT = "tokens/s"
 TICK_SEED_MODEL, TICK_SEED_STATE = 2024, 5
 
 
-def _tick_common(args):
-    world, rank, local = dist_env()
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
+def _init_dist(device, world):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=device)
-    if args.steps + max(args.warmup, 3) > 200:
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=device)
+
+
+def _tick_inputs(B, steps, warmup, device):
+    if steps + max(warmup, 3) > 200:
         raise SystemExit("smollm_tick: steps + warmup must stay within the 256 reserved tokens")
-    B = args.batch or 128
     cfg = W.smollm2_135m_config()
     model = W.seeded_llama(cfg, TICK_SEED_MODEL, torch.float16, device)
     blocks = W.tick_blocks(B, TICK_SEED_STATE)
     g = torch.Generator().manual_seed(99)
-    toks = torch.randint(0, cfg.vocab_size, (args.warmup + 2 * args.steps + 4, B), generator=g)
-    return world, rank, device, B, cfg, model, blocks, toks
+    toks = torch.randint(0, cfg.vocab_size, (warmup + 2 * steps + 4, B), generator=g)
+    return cfg, model, blocks, toks
 
 
 def _tick_bytes(cfg, lengths, model) -> float:
@@ -671,70 +865,116 @@ def _tick_e2e(runner, ids, toks, start, steps, device):
     return e0.elapsed_time(e1) / steps
 
 
-def run_tick(args):
-    world, rank, device, B, cfg, model, blocks, toks = _tick_common(args)
+def measure_tick(device, world, steps: int, warmup: int, B: int = 128) -> dict:
+    """One replica per GPU: the decode tick of the SmolLM2-135M architecture
+    through llama_runner.PagedLlama with graph-captured ticks, device time of
+    K replays (max over ranks), then K ticks end to end through
+    PagedLlama.decode with greedy sampling to the host."""
+    cfg, model, blocks, toks = _tick_inputs(B, steps, warmup, device)
     runner = PKG.PagedLlama(model, None, blocks=blocks, block_size=16, max_batch=B, graphs=True)
     ids, lengths = W.decode_tick_state(runner.cache, B, TICK_SEED_STATE)
-    for i in range(max(args.warmup, 3)):  # eager tick, capture, replays
+    for i in range(max(warmup, 3)):  # eager tick, capture, replays
         runner.decode(ids, toks[i].tolist())
     torch.cuda.synchronize(device)
     tick = runner._b200_graphs[B]
     with torch.inference_mode():  # the graph's buffers were made in inference mode
         tick.tokens.copy_(toks[0].view(B, 1))
-    # device time: the captured tick replayed back to back (inputs resident)
     clocks = ClockSampler(device.index)
     clocks.start()
     barrier(world, device)
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         tick.graph.replay()
     e1.record()
     e1.synchronize()
     clk = clocks.stop()
-    ms_tick = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
+    ms_tick = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
     # the replays advanced the device lengths past the host's: re-upload them
     runner.cache._rows = [None] * runner.cache.max_batch
     barrier(world, device)
-    ms_e2e = max_over_ranks(_tick_e2e(runner, ids, toks, max(args.warmup, 3), args.steps,
-                                      device), world, device)
+    ms_e2e = max_over_ranks(_tick_e2e(runner, ids, toks, max(warmup, 3), steps, device),
+                            world, device)
     ms_attn = _time_attention_share(runner, B, device)
-    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
-        REPO / "MEASURED_PEAKS.json").exists() else {}
-    peak = peaks.get("hbm_gbs") or 6650.0
-    nbytes = _tick_bytes(cfg, lengths + max(args.warmup, 3), model)
+    nbytes = _tick_bytes(cfg, lengths + max(warmup, 3), model)
+    res = {
+        "metric": TICK_METRIC, "value": world * B / (ms_tick * 1e-3), "unit": TICK_UNIT,
+        "ms_per_step": ms_tick, "scaling": "weak", "dtype": "f16",
+        "config": {"workload": "smollm2-135m decode tick: 30 layers, 9/3 heads, head_dim 64, "
+                               f"hidden 576, vocab 49152, batch {B} per GPU, lengths "
+                               "U[16,4096], pages reused in shuffled order, block 16",
+                   "batch_per_gpu": B, "mean_length": float(lengths.float().mean()),
+                   "parallelism": f"replica x{world}",
+                   "l2": "inputs larger than L2 (KV %.1f GB)" % (
+                       2 * runner.cache.keys.numel() * 2 / 1e9)},
+        "step": "one CUDA graph per tick: embedding, 30 x (norm, fused q/k/v GEMM, "
+                "decode_attention, o GEMM, MLP), norm, LM head",
+        "roofline": _roofline(nbytes / (ms_tick * 1e-3) / 1e9, "hbm",
+                              "whole tick (weights once + every cached K/V row once)",
+                              algorithmic_bytes_per_step=nbytes,
+                              attention_ms_per_step=ms_attn),
+        "clocks": clk,
+        "gpu_launches": steps * cfg.num_hidden_layers,
+        "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": TICK_UNIT,
+                "ms_per_step": ms_e2e, "h2d_bytes_per_step": B * 8,
+                "d2h_bytes_per_step": B * 8,
+                "path": "PagedLlama.decode(ids, tokens) per tick, greedy next token to "
+                        "the host"},
+    }
+    del runner, tick, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_tick_reference(device, steps: int, warmup: int, mod, B: int = 128) -> dict:
+    """The reference decode tick (worker/llama.py:151-177, restated and pinned
+    in oracle/llama_model.py) with its own CUDA attention kernel (or its torch
+    path when that kernel was not built), same model, state and loop."""
+    from oracle import llama_model as LM
+    cfg, model, blocks, toks = _tick_inputs(B, steps, warmup, device)
+    if mod is not None:
+        def attention(q, k, v, tables, lengths, max_length):
+            return mod.paged_attention(q.contiguous(), k, v, tables.contiguous(),
+                                       lengths.contiguous(), max_length)
+        which = "reference CUDA kernel (cuda/paged_attention.cu, built into oracle/_ref)"
+    else:
+        attention, which = None, "reference torch path (torch_paged_attention)"
+    runner = LM.PagedLlamaOracle(model, blocks=blocks, block_size=16, attention=attention)
+    ids, lengths = W.decode_tick_state(runner.cache, B, TICK_SEED_STATE)
+    for i in range(max(warmup, 3)):
+        runner.decode(ids, toks[i].tolist())
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    ms = _tick_e2e(runner, ids, toks, max(warmup, 3), steps, device)
+    clk = clocks.stop()
+    res = {"metric": TICK_METRIC, "value": B / (ms * 1e-3), "unit": TICK_UNIT,
+           "ms_per_step": ms, "scaling": "weak", "dtype": "f16",
+           "config": {"workload": "smollm2-135m decode tick", "batch_per_gpu": B,
+                      "attention": which, "parallelism": "replica x1"},
+           "clocks": clk,
+           "e2e": {"value": B / (ms * 1e-3), "unit": TICK_UNIT, "ms_per_step": ms,
+                   "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    del runner, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_tick(args):
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _init_dist(device, world)
+    B = args.batch or 128
+    if args.impl == "reference":
+        res = measure_tick_reference(device, args.steps, args.warmup, _reference_kernel_module(), B)
+        res["impl"] = "reference"
+    else:
+        res = measure_tick(device, world, args.steps, args.warmup, B)
     if rank == 0:
-        line = {
-            "metric": TICK_METRIC, "value": world * B / (ms_tick * 1e-3), "unit": TICK_UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
-            "ms_per_step": ms_tick, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic (seeded random-init weights and KV; no checkpoint)",
-            "config": {"workload": "smollm2-135m decode tick: 30 layers, 9/3 heads, head_dim 64, "
-                                   f"hidden 576, vocab 49152, batch {B} per GPU, lengths "
-                                   "U[16,4096], pages reused in shuffled order, block 16",
-                       "batch_per_gpu": B, "mean_length": float(lengths.float().mean()),
-                       "parallelism": f"replica x{world}",
-                       "step": "one CUDA graph per tick: embedding, 30 x (norm, q/k/v proj, "
-                               "rope_kv_write_decode, paged_attention, o proj, MLP), norm, "
-                               "LM head",
-                       "l2": "inputs larger than L2 (KV %.1f GB)" % (
-                           2 * runner.cache.keys.numel() * 2 / 1e9)},
-            "roofline": {"bound": "hbm", "achieved": nbytes / (ms_tick * 1e-3) / 1e9,
-                         "peak": peak, "unit": "GB/s",
-                         "frac": nbytes / (ms_tick * 1e-3) / 1e9 / peak, "traffic": None,
-                         "kernel": "whole tick (weights once + every cached K/V row once)",
-                         "algorithmic_bytes_per_step": nbytes,
-                         "attention_ms_per_step": ms_attn},
-            "clocks": clk,
-            "gpu_launches": args.steps * cfg.num_hidden_layers * 2,
-            "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": TICK_UNIT,
-                    "ms_per_step": ms_e2e, "h2d_bytes_per_step": B * 8,
-                    "d2h_bytes_per_step": B * 8,
-                    "path": "PagedLlama.decode(ids, tokens) per tick, greedy next token to "
-                            "the host"},
-        }
+        line = {"n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+                "higher_is_better": True, "vs_baseline": None,
+                "data": "synthetic (seeded random-init weights and KV; no checkpoint)", **res}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -762,55 +1002,13 @@ def _time_attention_share(runner, B, device, reps=10):
     return time_graph(g, reps, stream) / reps
 
 
-def run_tick_reference(args):
-    """The reference decode tick (worker/llama.py:151-177, restated and pinned
-    in oracle/llama_model.py) with its own CUDA attention kernel (or its torch
-    path when that kernel was not built), same model, state and loop."""
-    world, rank, device, B, cfg, model, blocks, toks = _tick_common(args)
-    from oracle import build_ref
-    from oracle import llama_model as LM
-    mod = build_ref.load_ref_module()
-    if mod is not None:
-        def attention(q, k, v, tables, lengths, max_length):
-            return mod.paged_attention(q.contiguous(), k, v, tables.contiguous(),
-                                       lengths.contiguous(), max_length)
-        which = "reference CUDA kernel (cuda/paged_attention.cu, built into oracle/_ref)"
-    else:
-        attention, which = None, "reference torch path (torch_paged_attention)"
-    runner = LM.PagedLlamaOracle(model, blocks=blocks, block_size=16, attention=attention)
-    ids, lengths = W.decode_tick_state(runner.cache, B, TICK_SEED_STATE)
-    for i in range(max(args.warmup, 3)):
-        runner.decode(ids, toks[i].tolist())
-    clocks = ClockSampler(device.index)
-    clocks.start()
-    barrier(world, device)
-    ms = max_over_ranks(_tick_e2e(runner, ids, toks, max(args.warmup, 3), args.steps, device),
-                        world, device)
-    clk = clocks.stop()
-    if rank == 0:
-        value = world * B / (ms * 1e-3)
-        print(json.dumps({
-            "metric": TICK_METRIC, "value": value, "unit": TICK_UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic (seeded random-init weights and KV; no checkpoint)",
-            "impl": "reference",
-            "config": {"workload": "smollm2-135m decode tick", "batch_per_gpu": B,
-                       "attention": which, "parallelism": f"replica x{world}"},
-            "clocks": clk,
-            "e2e": {"value": value, "unit": TICK_UNIT, "ms_per_step": ms,
-                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier(device_ids=[device.index])
-        dist.destroy_process_group()
-
-
 # --------------------------------------------------------------------------
 # prefill attention (16 prompts, SmolLM2 heads)
 # --------------------------------------------------------------------------
 PREFILL_METRIC = "prefill attention prompt tokens/s per layer (16 prompts, len U[64,1024])"
+# Independent copies of a prefill step's inputs; consecutive steps use
+# different copies, so the timed steps read more than L2 holds.
+L2_COPIES = 4
 
 
 def _prefill_case(device, B=16, H=9, KVH=3, D=64, bs=16, seed=4):
@@ -842,65 +1040,81 @@ def _prefill_case(device, B=16, H=9, KVH=3, D=64, bs=16, seed=4):
                 flops=flops, H=H, KVH=KVH, D=D)
 
 
+def _graph_of_steps(step_fns, steps, stream, device, warmup):
+    """One CUDA graph of `steps` steps, step i running step_fns[i % len]."""
+    with torch.cuda.stream(stream):
+        for _ in range(max(warmup, 1)):
+            for fn in step_fns:
+                fn()
+    torch.cuda.synchronize(device)
+
+    def run():
+        for i in range(steps):
+            step_fns[i % len(step_fns)]()
+    g = capture(run, stream)
+    time_graph(g, 1, stream)  # graph upload
+    return g
+
+
+def measure_prefill(device, steps: int, warmup: int, impl: str = "ours",
+                    kernel: str = "auto") -> dict:
+    cases = [_prefill_case(device) for _ in range(L2_COPIES)]
+    c0 = cases[0]
+    if impl == "reference":
+        import torch.nn.functional as F
+        groups = c0["H"] // c0["KVH"]
+
+        def make(c):
+            def step():  # worker/llama.py:141-144
+                ctx = F.scaled_dot_product_attention(
+                    c["q"].transpose(1, 2),
+                    c["k"].repeat_interleave(groups, dim=2).transpose(1, 2),
+                    c["v"].repeat_interleave(groups, dim=2).transpose(1, 2), is_causal=True)
+                return ctx.transpose(1, 2).reshape(c["q"].shape[0], c["q"].shape[1], -1)
+            return step
+        which = "reference prefill attention: repeat_interleave + causal SDPA on the padded batch"
+    else:
+        impl_id = {"auto": PKG.PREFILL_AUTO, "tcgen05": PKG.PREFILL_TCGEN05,
+                   "mma": PKG.PREFILL_MMA}[kernel]
+
+        def make(c):
+            out = torch.empty_like(c["q"])
+
+            def step():
+                return PKG.prefill_attention(c["q"], c["k_pool"], c["v_pool"], c["tables"],
+                                             c["lengths"], out=out, impl=impl_id)
+            return step
+        which = ("prefill_attention_kernel<64> (mma.sync; K/V from the paged pools)"
+                 if kernel == "mma" else
+                 "prefill_tc_kernel<64> (tcgen05.mma + TMEM, TMA from the paged pools)")
+    stream = torch.cuda.Stream(device)
+    g = _graph_of_steps([make(c) for c in cases], steps, stream, device, warmup)
+    ms, clk, reps = timed_replays(g.replay, stream, device, steps)
+    tflops = c0["flops"] / (ms * 1e-3) / 1e12
+    res = {"metric": PREFILL_METRIC, "value": c0["tokens"] / (ms * 1e-3), "unit": "tokens/s",
+           "ms_per_step": ms, "scaling": "replicas only", "dtype": "f16",
+           "config": {"workload": "prefill attention: 16 prompts, len U[64,1024], heads 9/3, "
+                                  "head_dim 64, block 16, one layer per step",
+                      "prompt_tokens": c0["tokens"],
+                      "l2": f"{L2_COPIES} input copies used in turn (inputs larger than L2)"},
+           "timing": f"median of {reps} CUDA-event-timed replays of a {steps}-step graph",
+           "roofline": _roofline(tflops, "tensor", which, algorithmic_flops_per_step=c0["flops"],
+                                 note="causal FLOPs only (QK and PV over keys <= query)"),
+           "clocks": clk, "gpu_launches": steps if impl != "reference" else None}
+    del g, cases
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_prefill(args):
     world, rank, local = dist_env()
     if rank != 0:
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    c = _prefill_case(device)
-    if args.impl == "reference":
-        import torch.nn.functional as F
-        groups = c["H"] // c["KVH"]
-
-        def step():  # worker/llama.py:141-144
-            ctx = F.scaled_dot_product_attention(
-                c["q"].transpose(1, 2), c["k"].repeat_interleave(groups, dim=2).transpose(1, 2),
-                c["v"].repeat_interleave(groups, dim=2).transpose(1, 2), is_causal=True)
-            return ctx.transpose(1, 2).reshape(c["q"].shape[0], c["q"].shape[1], -1)
-        which = "reference prefill attention: repeat_interleave + causal SDPA on the padded batch"
-    else:
-        out = torch.empty_like(c["q"])
-        impl = {"auto": PKG.PREFILL_AUTO, "tcgen05": PKG.PREFILL_TCGEN05,
-                "mma": PKG.PREFILL_MMA}[args.prefill_kernel]
-
-        def step():
-            return PKG.prefill_attention(c["q"], c["k_pool"], c["v_pool"], c["tables"],
-                                         c["lengths"], out=out, impl=impl)
-        which = ("prefill_attention_kernel<64> (mma.sync; K/V from the paged pools)"
-                 if args.prefill_kernel == "mma" else
-                 "prefill_tc_kernel<64> (tcgen05.mma + TMEM, TMA from the paged pools)")
-    stream = torch.cuda.Stream(device)
-    with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
-            step()
-    torch.cuda.synchronize(device)
-
-    def steps():  # the K timed steps back to back in one graph: one launch gap per run, not per step
-        for _ in range(args.steps):
-            step()
-    g = capture(steps, stream)
-    time_graph(g, 1, stream)  # graph upload
-    clocks = ClockSampler(device.index)
-    clocks.start()
-    ms = time_graph(g, 1, stream) / args.steps
-    clk = clocks.stop()
-    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
-        REPO / "MEASURED_PEAKS.json").exists() else {}
-    peak = peaks.get("bf16_tflops") or 1590.0
-    tflops = c["flops"] / (ms * 1e-3) / 1e12
-    line = {"metric": PREFILL_METRIC, "value": c["tokens"] / (ms * 1e-3), "unit": "tokens/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
-            "dtype": "f16", "data": "synthetic (seeded)",
-            "config": {"workload": "prefill attention: 16 prompts, len U[64,1024], heads 9/3, "
-                                   "head_dim 64, block 16, one layer per step",
-                       "kernel": which, "prompt_tokens": c["tokens"]},
-            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak,
-                         "unit": "TFLOP/s", "frac": tflops / peak, "traffic": None,
-                         "algorithmic_flops_per_step": c["flops"],
-                         "note": "causal FLOPs only (QK and PV over keys <= query)"},
-            "clocks": clk, "gpu_launches": args.steps if args.impl != "reference" else None}
+    res = measure_prefill(device, args.steps, args.warmup, args.impl, args.prefill_kernel)
+    line = {"n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "higher_is_better": True, "vs_baseline": None, "data": "synthetic (seeded)", **res}
     if args.impl == "reference":
         line["impl"] = "reference"
     print(json.dumps(line), flush=True)
@@ -910,86 +1124,121 @@ PREFILL_WRITE_METRIC = ("prefill RoPE + paged KV write prompt tokens/s per layer
                         "(16 prompts, len U[64,1024])")
 
 
-def run_prefill_write(args):
+def measure_prefill_write(device, steps: int, warmup: int, impl: str = "ours") -> dict:
     """Prefill RoPE + paged KV-slot write of one layer (worker/llama.py:128-140),
     16 SmolLM2-shaped prompts padded to the longest, into a 4096-block pool.
-    Ours: rope_kv_write with the valid mask (one varlen launch). Reference
-    arm: the reference's torch steps on the same GPU — RoPE of the padded q/k
-    with every op in FP16 (worker/llama.py:108-117) and
-    pool[slots] = k[valid], v[valid] (:138-140); the valid rows' flat indices
-    are computed once, outside the timed steps."""
+    Ours: rope_kv_write with the valid mask (one varlen launch). Reference:
+    the reference's torch steps on the same GPU — RoPE of the padded q/k with
+    every op in FP16 (worker/llama.py:108-117) and pool[slots] = k[valid],
+    v[valid] (:138-140); the valid rows' flat indices are computed once,
+    outside the timed steps."""
+    pw = W.prefill_smollm()
+    copies = [W.materialize_prefill(pw, device) for _ in range(L2_COPIES)]
+    d0 = copies[0]
+    B, Wd, H, D = d0["q"].shape
+    KVH = d0["k"].shape[2]
+    e = d0["q"].element_size()
+    ntok = int(pw.lengths.sum())
+    nbytes = ((2 * B * Wd * H * D + 3 * B * Wd * KVH * D) * e  # read q, k, v; write q', k'
+              + 2 * ntok * KVH * D * e + B * Wd)                # k, v slot writes; mask
+    if impl == "reference":
+        def rot(x):
+            a, b = x.chunk(2, dim=-1)
+            return torch.cat((-b, a), dim=-1)
+
+        def make(d):
+            vidx = d["valid"].reshape(-1).nonzero()[:, 0]
+            q_o, k_o = torch.empty_like(d["q"]), torch.empty_like(d["k"])
+
+            def step():
+                f = d["positions"].float()[..., None] * d["inv_freq"]
+                ang = torch.cat((f, f), dim=-1)
+                cos = ang.cos().to(d["q"].dtype).unsqueeze(2)
+                sin = ang.sin().to(d["q"].dtype).unsqueeze(2)
+                torch.add(d["q"] * cos, rot(d["q"]) * sin, out=q_o)
+                torch.add(d["k"] * cos, rot(d["k"]) * sin, out=k_o)
+                d["k_pool"][d["physical"], d["offsets"]] = k_o.view(-1, KVH, D)[vidx]
+                d["v_pool"][d["physical"], d["offsets"]] = d["v"].view(-1, KVH, D)[vidx]
+            return step
+        which = "reference prefill RoPE (torch ops in FP16) + index_put of the valid rows"
+    else:
+        def make(d):
+            q_o, k_o = torch.empty_like(d["q"]), torch.empty_like(d["k"])
+
+            def step():
+                PKG.rope_kv_write(d["q"], d["k"], d["v"], d["k_pool"], d["v_pool"],
+                                  d["physical"], d["offsets"], d["positions"], d["inv_freq"],
+                                  valid=d["valid"], q_out=q_o, k_out=k_o)
+            return step
+        which = "rope_kv_write_vec_kernel + valid_scan_kernel (varlen scatter into the pages)"
+    stream = torch.cuda.Stream(device)
+    g = _graph_of_steps([make(d) for d in copies], steps, stream, device, warmup)
+    ms, clk, reps = timed_replays(g.replay, stream, device, steps)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    res = {"metric": PREFILL_WRITE_METRIC, "value": ntok / (ms * 1e-3), "unit": "tokens/s",
+           "ms_per_step": ms, "scaling": "replicas only", "dtype": "f16",
+           "config": {"workload": "prefill RoPE + KV write: 16 prompts, len U[64,1024], heads "
+                                  "9/3, head_dim 64, block 16, 4096-block pool, one layer per "
+                                  "step", "prompt_tokens": ntok,
+                      "l2": f"{L2_COPIES} input copies used in turn (inputs larger than L2)"},
+           "timing": f"median of {reps} CUDA-event-timed replays of a {steps}-step graph",
+           "roofline": _roofline(gbs, "hbm", which, algorithmic_bytes_per_step=nbytes,
+                                 note="padded q, k, v read and q', k' written; valid rows' "
+                                      "k/v slots"),
+           "clocks": clk, "gpu_launches": 2 * steps if impl != "reference" else None}
+    del g, copies
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_prefill_write(args):
     world, rank, local = dist_env()
     if rank != 0:
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    pw = W.prefill_smollm()
-    d = W.materialize_prefill(pw, device)
-    B, Wd, H, D = d["q"].shape
-    KVH = d["k"].shape[2]
-    e = d["q"].element_size()
-    ntok = int(pw.lengths.sum())
-    nbytes = ((2 * B * Wd * H * D + 3 * B * Wd * KVH * D) * e  # read q, k, v; write q', k'
-              + 2 * ntok * KVH * D * e + B * Wd)                # k, v slot writes; mask
-    if args.impl == "reference":
-        vidx = d["valid"].reshape(-1).nonzero()[:, 0]
-        q_o, k_o = torch.empty_like(d["q"]), torch.empty_like(d["k"])
-
-        def rot(x):
-            a, b = x.chunk(2, dim=-1)
-            return torch.cat((-b, a), dim=-1)
-
-        def step():
-            f = d["positions"].float()[..., None] * d["inv_freq"]
-            ang = torch.cat((f, f), dim=-1)
-            cos = ang.cos().to(d["q"].dtype).unsqueeze(2)
-            sin = ang.sin().to(d["q"].dtype).unsqueeze(2)
-            torch.add(d["q"] * cos, rot(d["q"]) * sin, out=q_o)
-            torch.add(d["k"] * cos, rot(d["k"]) * sin, out=k_o)
-            d["k_pool"][d["physical"], d["offsets"]] = k_o.view(-1, KVH, D)[vidx]
-            d["v_pool"][d["physical"], d["offsets"]] = d["v"].view(-1, KVH, D)[vidx]
-        which = "reference prefill RoPE (torch ops in FP16) + index_put of the valid rows"
-    else:
-        q_o, k_o = torch.empty_like(d["q"]), torch.empty_like(d["k"])
-
-        def step():
-            PKG.rope_kv_write(d["q"], d["k"], d["v"], d["k_pool"], d["v_pool"], d["physical"],
-                              d["offsets"], d["positions"], d["inv_freq"], valid=d["valid"],
-                              q_out=q_o, k_out=k_o)
-        which = "rope_kv_write_vec_kernel + valid_scan_kernel (varlen scatter into the pages)"
-    stream = torch.cuda.Stream(device)
-    with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
-            step()
-    torch.cuda.synchronize(device)
-
-    def steps():  # the K timed steps back to back in one graph
-        for _ in range(args.steps):
-            step()
-    g = capture(steps, stream)
-    time_graph(g, 1, stream)
-    clocks = ClockSampler(device.index)
-    clocks.start()
-    ms = time_graph(g, 1, stream) / args.steps
-    clk = clocks.stop()
-    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
-        REPO / "MEASURED_PEAKS.json").exists() else {}
-    peak = peaks.get("hbm_gbs") or 6650.0
-    gbs = nbytes / (ms * 1e-3) / 1e9
-    line = {"metric": PREFILL_WRITE_METRIC, "value": ntok / (ms * 1e-3), "unit": "tokens/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
-            "dtype": "f16", "data": "synthetic (seeded)",
-            "config": {"workload": "prefill RoPE + KV write: 16 prompts, len U[64,1024], heads "
-                                   "9/3, head_dim 64, block 16, 4096-block pool, one layer per step",
-                       "kernel": which, "prompt_tokens": ntok},
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
-                         "frac": gbs / peak, "traffic": None, "algorithmic_bytes_per_step": nbytes,
-                         "note": "padded q, k, v read and q', k' written; valid rows' k/v slots"},
-            "clocks": clk, "gpu_launches": 2 * args.steps if args.impl != "reference" else None}
+    res = measure_prefill_write(device, args.steps, args.warmup, args.impl)
+    line = {"n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "higher_is_better": True, "vs_baseline": None, "data": "synthetic (seeded)", **res}
     if args.impl == "reference":
         line["impl"] = "reference"
     print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# the other configurations, measured in the same run as the headline
+# --------------------------------------------------------------------------
+def secondary_ours(args, device, world) -> dict:
+    """Every other configuration in the same run, each with its own CUDA-event
+    time, roofline figure and clock record. At N = 1: the SmolLM2 decode in
+    FP16 (30 pools) and FP32, the prefill RoPE + KV write, the prefill
+    attention and the decode tick. At N > 1 the decode tick alone, one replica
+    per GPU (weak scaling, max over ranks)."""
+    out = {}
+    steps, warmup = args.steps, args.warmup
+    if world == 1:
+        out["smollm_fp16"] = measure_decode(W.smollm_fp16(), device, steps, warmup)
+        out["smollm_fp32"] = measure_decode(W.smollm_fp32(), device, steps, warmup)
+        out["prefill_write"] = measure_prefill_write(device, steps, warmup)
+        out["prefill_attention"] = measure_prefill(device, steps, warmup)
+    out["decode_tick"] = measure_tick(device, world, min(steps, 100), warmup)
+    return out
+
+
+def secondary_reference(args, device, mod) -> dict:
+    """The reference's own code for the same configurations, on the same GPU:
+    its decode layer (torch RoPE, slot writes, its CUDA kernel) for the
+    SmolLM2 shapes, its prefill RoPE + slot writes and prefill attention in
+    torch, and its PagedLlama.decode tick with its CUDA kernel."""
+    out = {}
+    steps, warmup = args.steps, args.warmup
+    if mod is not None:
+        out["smollm_fp16"] = measure_decode_reference(W.smollm_fp16(), device, 3, mod)
+        out["smollm_fp32"] = measure_decode_reference(W.smollm_fp32(), device, 3, mod)
+    out["prefill_write"] = measure_prefill_write(device, steps, warmup, "reference")
+    out["prefill_attention"] = measure_prefill(device, steps, warmup, "reference")
+    out["decode_tick"] = measure_tick_reference(device, min(steps, 10), warmup, mod)
+    return out
 
 
 def main():
@@ -999,7 +1248,7 @@ def main():
     elif args.workload == "prefill_write":
         run_prefill_write(args)
     elif args.workload == "smollm_tick":
-        (run_tick_reference if args.impl == "reference" else run_tick)(args)
+        run_tick(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -8,6 +8,8 @@ measured on:
                  head_dim 64, block 16, 256-block pool, len ~ U[1, 512], theta 1e5
   smollm_fp16    same shape, FP16, batch 64, len ~ U[128, 2048], 30 layers, pool =
                  1.25 x blocks needed, unused blocks hold stale N(0, 4) values
+  smollm_fp32    the same batch, lengths and tables in FP32 (the CPU shape's
+                 dtype at GPU size)
   llama3_8b      32/8 heads, head_dim 128, 32 layers, FP16, batch 256,
                  len ~ lognormal(median 1024, sigma 0.8) clipped to [16, 8192],
                  theta 5e5, fragmented tables, sequences sharded over ranks
@@ -159,14 +161,23 @@ def smollm_cpu(seed: int = 1) -> DecodeWorkload:
                           lengths, tables, n, used, stale_scale=1.0)
 
 
-def smollm_fp16(seed: int = 2, batch: int = 64, layers: int = 30) -> DecodeWorkload:
+def smollm_fp16(seed: int = 2, batch: int = 64, layers: int = 30,
+                dtype: torch.dtype = torch.float16) -> DecodeWorkload:
     """SmolLM2-135M shape in FP16: batch 64, len ~ U[128, 2048], 30 layers."""
     g = torch.Generator().manual_seed(seed)
     lengths = torch.randint(128, 2049, (batch,), generator=g, dtype=torch.int64).to(torch.int32)
     tables, n, used = make_decode_tables(lengths, 16, seed + 100, 1.25, None)
-    return DecodeWorkload("smollm2-135m-fp16", batch, 9, 3, 64, layers, 16, torch.float16, 1e5,
+    name = "smollm2-135m-fp16" if dtype == torch.float16 else "smollm2-135m-fp32"
+    return DecodeWorkload(name, batch, 9, 3, 64, layers, 16, dtype, 1e5,
                           seed, lengths, tables, n, used, stale_scale=2.0,
                           meta={"pool_factor": 1.25})
+
+
+def smollm_fp32(seed: int = 2, batch: int = 64, layers: int = 30) -> DecodeWorkload:
+    """The FP32 decode of the SmolLM2-135M CPU shape (9/3 heads, head_dim 64,
+    FP32) at the FP16 configuration's GPU size: batch 64, len ~ U[128, 2048],
+    30 layers, the same lengths and tables as smollm_fp16."""
+    return smollm_fp16(seed, batch, layers, dtype=torch.float32)
 
 
 def llama3_8b(seed: int = 3, batch: int = 256, layers: int = 32) -> DecodeWorkload:
