@@ -75,8 +75,12 @@ struct AttnParams {
   // fused decode step), so the launch may read them (plan, page lookups; K/V
   // tiles) before its programmatic-dependent-launch wait.
   int stable_meta;
-  int64_t q_row;   // fused: elements between consecutive sequences' q rows (H * D if packed)
+  int64_t q_row;   // elements between consecutive sequences' q rows (H * D if packed)
   int64_t kv_row;  // fused: same for k_new / v_new (KVH * D if packed)
+  // Dynamic TMA kernel: q (and, fused, k_new / v_new) rows and strides are
+  // 16-byte aligned, so the producer warp may bulk-copy a piece's q rows and
+  // new-token rows into shared memory along with its first tile.
+  int bulk_q;
 };
 
 // Clamp a length read from device memory into [0, max_length].
@@ -412,6 +416,25 @@ struct MmaMath {
     for (int ks = 0; ks < KSTEPS; ++ks) {
       s.qb[ks][0] = real ? __ldg(reinterpret_cast<const unsigned*>(qrow + 16 * ks + 2 * tg)) : 0u;
       s.qb[ks][1] = real ? __ldg(reinterpret_cast<const unsigned*>(qrow + 16 * ks + 2 * tg + 8)) : 0u;
+    }
+    s.m[0] = s.m[1] = -INFINITY;
+    s.l[0] = s.l[1] = 0.f;
+#pragma unroll
+    for (int i = 0; i < KSTEPS; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s.acc[i][j] = 0.f;
+  }
+
+  // begin_piece with the group's G query rows (D halves each, consecutive)
+  // at `qbase`, in global or shared memory.
+  __device__ static void begin_piece_at(State& s, const __half* qbase, int G) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    const bool real = g < G;  // columns >= G are padding (q = 0)
+    const __half* qrow = qbase + (real ? g : 0) * D;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+      s.qb[ks][0] = real ? *reinterpret_cast<const unsigned*>(qrow + 16 * ks + 2 * tg) : 0u;
+      s.qb[ks][1] = real ? *reinterpret_cast<const unsigned*>(qrow + 16 * ks + 2 * tg + 8) : 0u;
     }
     s.m[0] = s.m[1] = -INFINITY;
     s.l[0] = s.l[1] = 0.f;

@@ -111,7 +111,8 @@ __device__ __forceinline__ int64_t claim_chunk(unsigned long long* ctr, unsigned
 // after them, each group in index order; with no tail the order is the index
 // order. Three block passes over the lengths: the unit total (which fixes the
 // plan and the threshold), the long sequences' count and units, and a prefix
-// scan placing every sequence. All NT threads call it; misc holds
+// scan placing every sequence; the lengths are read from global memory once,
+// into Lidx (by sequence index). All NT threads call it; misc holds
 // 3 + 3 * NT / 32 ints.
 __device__ __forceinline__ void warp_scan3(int& a, int& b, int& c, int lane) {
 #pragma unroll
@@ -128,17 +129,17 @@ __device__ __forceinline__ void warp_scan3(int& a, int& b, int& c, int lane) {
 }
 
 template <int NT>
-__device__ int64_t plan_dyn_stream(const AttnParams& p, int* P, int* Ls, int* ord, int* misc,
-                                   int64_t launched, int tile_units, DynPlan& pl) {
+__device__ int64_t plan_dyn_stream(const AttnParams& p, int* P, int* Ls, int* ord, int* Lidx,
+                                   int* misc, int64_t launched, int tile_units, DynPlan& pl) {
   constexpr int NWARP = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int B = p.B, KVH = p.KVH;
   auto units_of = [&](int len) { return (len + kUnitTokens - 1) / kUnitTokens; };
-  // pass 1: unit total (lengths kept by index in Ls for pass 2)
+  // pass 1: unit total (lengths kept by index in Lidx)
   int part = 0;
   for (int b = tid; b < B; b += NT) {
     const int len = checked_length(p.lengths, b, p.max_length);
-    Ls[b] = len;
+    Lidx[b] = len;
     part += units_of(len) * KVH;
   }
 #pragma unroll
@@ -155,7 +156,7 @@ __device__ int64_t plan_dyn_stream(const AttnParams& p, int* P, int* Ls, int* or
   // pass 2: long sequences' count and units
   int fc = 0, fu = 0;
   for (int b = tid; b < B; b += NT) {
-    const int nu = units_of(Ls[b]);
+    const int nu = units_of(Lidx[b]);
     if (nu > thr) {
       ++fc;
       fu += nu * KVH;
@@ -178,13 +179,13 @@ __device__ int64_t plan_dyn_stream(const AttnParams& p, int* P, int* Ls, int* or
     NL += misc[3 + NWARP + w];
   }
   __syncthreads();
-  // pass 3: place every sequence (lengths re-read: Ls is rewritten by position)
+  // pass 3: place every sequence
   int off_f = 0, off_fu = 0, off_a = 0;
   for (int base = 0; base < B; base += NT) {
     const int b = base + tid;
     int len = 0, nu = 0, f = 0;
     if (b < B) {
-      len = checked_length(p.lengths, b, p.max_length);
+      len = Lidx[b];
       nu = units_of(len) * KVH;
       f = units_of(len) > thr ? 1 : 0;
     }
@@ -245,6 +246,9 @@ struct TileRecord {
 // segment's last unit, i.e. the new token; kRecNewRow: this tile holds it.
 constexpr int kRecFirst = 1, kRecLast = 2, kRecWhole = 4, kRecEnd = 8, kRecOpen = 16;
 constexpr int kRecNewTok = 32, kRecNewRow = 64;
+// kRecQPre: the piece that starts here has its q rows (and, with kRecNewTok,
+// the new token's k and v rows) in the stage's prefetch slots.
+constexpr int kRecQPre = 128;
 
 // Work queued by the math warps for the epilogue warp: the tag install of a
 // piece's counter when the piece starts, its arrival when it ends, the end.
@@ -262,24 +266,26 @@ constexpr int kDynMisc = 32;  // ints of per-CTA scratch
 
 // Fused decode prologue at the start of a piece (all math threads, tid <
 // NW * 32), in place of MmaMath::begin_piece: the lane's q elements and — for
-// the piece holding the new token — the token's k and v are loaded first, so
-// their latency overlaps the piece's cos/sin table (FP16-rounded, as
-// rope_kv_write computes them; inv_freq staged in shared memory); then q is
-// rotated into the lane's Q^T fragment (rotate-half: element i < D/2 pairs
-// with i + D/2) and the token's rotated k and its v go to `newrow`, from where
-// the tile holding the token is patched and the pool slot written. Per-op
-// FP16 rounding as in rope_kv_write. `sync` is a barrier over the math threads.
+// the piece holding the new token — the token's k and v are read first (from
+// the stage's prefetch slots, or from global memory, so their latency
+// overlaps the piece's cos/sin table: FP16-rounded, as rope_kv_write computes
+// them; inv_freq staged in shared memory); then q is rotated into the lane's
+// Q^T fragment (rotate-half: element i < D/2 pairs with i + D/2) and the
+// token's rotated k and its v go to `newrow`, from where the tile holding the
+// token is patched and the pool slot written. Per-op FP16 rounding as in
+// rope_kv_write. `qbase` points at the group's G query rows, `knew` / `vnew`
+// at the token's k and v rows. `sync` is a barrier over the math threads.
 template <class M, class Sync>
 __device__ __forceinline__ void fused_piece_start(typename M::State& st, const AttnParams& p,
-                                                  int b, int h, int pos, bool new_tok,
+                                                  const __half* qbase, const __half* knew,
+                                                  const __half* vnew, int pos, bool new_tok,
                                                   const float* invf, float* cs, __half* newrow,
                                                   Sync sync) {
   constexpr int D = M::D, KS = M::KSTEPS, HALF = D / 2;
   static_assert(KS % 2 == 0, "lower and upper halves in whole k-steps");
   const int tid = threadIdx.x, lane = tid & 31, g = lane >> 2, tg = lane & 3;
   const bool real = g < p.G;  // columns >= G are padding (q = 0)
-  const __half* qrow = static_cast<const __half*>(p.q) + (int64_t)b * p.q_row +
-                       ((int64_t)h * p.G + (real ? g : 0)) * D;
+  const __half* qrow = qbase + (real ? g : 0) * D;
   __half2 qx1[KS / 2][2], qx2[KS / 2][2];
 #pragma unroll
   for (int ks = 0; ks < KS / 2; ++ks)
@@ -290,12 +296,11 @@ __device__ __forceinline__ void fused_piece_start(typename M::State& st, const A
       qx2[ks][r] = *reinterpret_cast<const __half2*>(qrow + i + HALF);
     }
   __half k1 = __float2half_rn(0.f), k2 = k1, v1 = k1, v2 = k1;
-  const int64_t src = (int64_t)b * p.kv_row + (int64_t)h * D;
   if (new_tok && tid < HALF) {
-    k1 = static_cast<const __half*>(p.k_new)[src + tid];
-    k2 = static_cast<const __half*>(p.k_new)[src + tid + HALF];
-    v1 = static_cast<const __half*>(p.v_new)[src + tid];
-    v2 = static_cast<const __half*>(p.v_new)[src + tid + HALF];
+    k1 = knew[tid];
+    k2 = knew[tid + HALF];
+    v1 = vnew[tid];
+    v2 = vnew[tid + HALF];
   }
   if (tid < HALF) {
     float c, s;
@@ -357,10 +362,16 @@ struct DynStreamK {
   static constexpr int NT = (NW + 2) * 32;  // math warps, producer, epilogue
   static constexpr int HALVES = D / 64;
   static constexpr int UNIT_BYTES = 2 * kUnitTokens * D * 2;
-  static constexpr int MERGE_FLOATS = NW * GP * (D + 2);
+  // Per-stage prefetch slots: a piece's q rows (G <= GP rows of D halves)
+  // and the new token's k and v rows.
+  static constexpr int QPRE_BYTES = GP * D * 2;
+  static constexpr int KVPRE_BYTES = 2 * D * 2;
+  // At a piece end the warps' partial states (m, l, O per head) go through
+  // the buffer of the stage just consumed.
+  static_assert(NW * GP * (D + 2) * 4 <= M::STAGE_BYTES, "merge area fits in a stage");
   static size_t smem_bytes(int B) {
-    return 1024 + (size_t)STAGES * M::STAGE_BYTES + (size_t)MERGE_FLOATS * 4 +
-           (size_t)(3 * B + 1 + kDynMisc) * 4 + (2 * STAGES + 2 * kHandoffDepth) * 8 + 16 +
+    return 1024 + (size_t)STAGES * (M::STAGE_BYTES + QPRE_BYTES + KVPRE_BYTES) +
+           (size_t)(4 * B + 1 + kDynMisc) * 4 + (2 * STAGES + 2 * kHandoffDepth) * 8 + 16 +
            (size_t)STAGES * sizeof(TileRecord) + kHandoffDepth * sizeof(PieceHandoff) +
            (size_t)D * 4 + (size_t)2 * D * 2 + (size_t)D / 2 * 4 +
            64;  // + fused prologue: cos/sin, new row, inv_freq (+ alignment)
@@ -384,13 +395,13 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* ms = reinterpret_cast<float*>(smem + (size_t)STAGES * M::STAGE_BYTES);
-  float* ls = ms + NW * GP;
-  float* accs = ls + NW * GP;
-  int* P = reinterpret_cast<int*>(accs + NW * GP * D);  // by stream position
+  unsigned char* qpre = smem + (size_t)STAGES * M::STAGE_BYTES;  // [STAGES][QPRE_BYTES]
+  unsigned char* kvpre = qpre + (size_t)STAGES * K::QPRE_BYTES;  // [STAGES][KVPRE_BYTES]
+  int* P = reinterpret_cast<int*>(kvpre + (size_t)STAGES * K::KVPRE_BYTES);  // by stream position
   int* Ls = P + p.B + 1;
   int* ord = Ls + p.B;
-  int* misc = ord + p.B;  // [kDynMisc]
+  int* Lidx = ord + p.B;  // lengths by sequence index (plan only)
+  int* misc = Lidx + p.B;  // [kDynMisc]
   uint64_t* bars = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(misc + kDynMisc) + 7) & ~uintptr_t(7));
   uint64_t* full = bars;
@@ -438,7 +449,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
   }
   static_assert(3 + 3 * (NT / 32) <= kDynMisc, "plan scratch");
   DynPlan pl;
-  const int64_t U = plan_dyn_stream<NT>(p, P, Ls, ord, misc, gridDim.x, TU, pl);
+  const int64_t U = plan_dyn_stream<NT>(p, P, Ls, ord, Lidx, misc, gridDim.x, TU, pl);
   if (early && warp != NW) grid_dependency_wait();  // math and epilogue warps
   if (warp < NW) {  // zero rows of empty sequences (the producer warp may not have waited)
     for (int i = blockIdx.x; i < p.B; i += gridDim.x) {
@@ -496,6 +507,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
         const int tok0 = (int)(c.u - c.seg) * kUnitTokens;
         const bool seg_end = te == c.seg + c.nu;
         const bool last = seg_end || te == we;
+        const bool new_tok = FUSE && piece_first && c.seg + c.nu <= we;
         if (lane == 0) {
           TileRecord r{};
           r.b = ord[c.b];
@@ -505,7 +517,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
           r.ntok = nunits * kUnitTokens < rem ? nunits * kUnitTokens : rem;
           r.flags = (piece_first ? kRecFirst : 0) | (last ? kRecLast : 0);
           if (piece_first && !(c.u == c.seg && c.seg + c.nu <= we)) r.flags |= kRecOpen;
-          if (FUSE && piece_first && c.seg + c.nu <= we) r.flags |= kRecNewTok;
+          if (new_tok) r.flags |= kRecNewTok;
           if (FUSE && seg_end) r.flags |= kRecNewRow;
           if (last) {
             // The piece started at the worker's begin or at the segment's.
@@ -550,10 +562,34 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
                                      : -1;
           }
         }
-        if (!early_kv) wait_prev();
+        // With stable pools the first STAGES tiles are issued before the
+        // dependency wait; the producer would block on a stage release after
+        // them anyway, so it waits there.
+        if (!early_kv || k >= STAGES) wait_prev();
+        // A piece's q rows (and the new token's k and v) ride on its first
+        // tile's barrier, once the previous kernel (which may have written
+        // them) is complete; before that, the math warps read them from
+        // global memory themselves.
+        const bool qp = p.bulk_q != 0 && waited && piece_first;
+        const bool kvp = qp && new_tok;
         if (lane == 0) {
+          const int qbytes = p.G * D * 2;
+          if (qp) recs[s].flags |= kRecQPre;
           fence_proxy_async_smem();
-          mbar_arrive_expect_tx(&full[s], (uint32_t)__popc(okmask) * K::UNIT_BYTES);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)__popc(okmask) * K::UNIT_BYTES +
+                                              (qp ? qbytes : 0) + (kvp ? K::KVPRE_BYTES : 0));
+          const int bq = ord[c.b];
+          if (qp)
+            bulk_load(qpre + (size_t)s * K::QPRE_BYTES,
+                      static_cast<const __half*>(p.q) + (int64_t)bq * p.q_row +
+                          (int64_t)c.h * p.G * D,
+                      (uint32_t)qbytes, &full[s]);
+          if (kvp) {
+            const int64_t kvo = (int64_t)bq * p.kv_row + (int64_t)c.h * D;
+            unsigned char* dst = kvpre + (size_t)s * K::KVPRE_BYTES;
+            bulk_load(dst, static_cast<const __half*>(p.k_new) + kvo, D * 2, &full[s]);
+            bulk_load(dst + D * 2, static_cast<const __half*>(p.v_new) + kvo, D * 2, &full[s]);
+          }
         }
         __syncwarp();
         if (ok) {
@@ -646,10 +682,19 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
     unsigned char* sk = stage_k(s);
     unsigned char* sv = sk + M::TILE_BYTES;
     const int r0 = warp * M::WT;
+    const bool pre = (r.flags & kRecQPre) != 0;
+    const __half* qbase =
+        pre ? reinterpret_cast<const __half*>(qpre + (size_t)s * K::QPRE_BYTES)
+            : static_cast<const __half*>(p.q) + (int64_t)r.b * p.q_row + (int64_t)r.h * p.G * D;
     if constexpr (FUSE) {
-      if (r.flags & kRecFirst)
-        fused_piece_start<M>(st, p, r.b, r.h, r.len - 1, (r.flags & kRecNewTok) != 0, invf,
-                             cs_tab, newrow, sync_math);
+      if (r.flags & kRecFirst) {
+        const __half* kvs = reinterpret_cast<const __half*>(kvpre + (size_t)s * K::KVPRE_BYTES);
+        const int64_t kvo = (int64_t)r.b * p.kv_row + (int64_t)r.h * D;
+        fused_piece_start<M>(st, p, qbase, pre ? kvs : static_cast<const __half*>(p.k_new) + kvo,
+                             pre ? kvs + D : static_cast<const __half*>(p.v_new) + kvo,
+                             r.len - 1, (r.flags & kRecNewTok) != 0, invf, cs_tab, newrow,
+                             sync_math);
+      }
       // The new token's row of this tile: the TMA brought the slot's old
       // bytes; the owning warp writes the rotated k and the v in their place
       // and into the pool slot (for later steps; this launch never reads the
@@ -684,45 +729,80 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
     if ((r.flags & (kRecFirst | kRecOpen)) == (kRecFirst | kRecOpen))
       hand_off(PieceHandoff{0, 0, r.b, r.h, 0, 0, kHandInstall, 0});
     if (r.flags & kRecFirst) {
-      if constexpr (!FUSE) M::begin_piece(st, p, r.b, r.h);  // fused: done above
+      if constexpr (!FUSE) M::begin_piece_at(st, qbase, p.G);  // fused: done above
     }
     M::compute_tile(st, p, sk, sv, r.ntok, nullptr);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-
-    if (r.flags & kRecLast) {
-      M::store_state(st, ms, ls, accs);
-      sync_math();
+    if (!(r.flags & kRecLast)) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      continue;
+    }
+    // Piece end. Once every math warp is done with the tile, the stage's
+    // buffer holds the warps' partial states (m, l, O per head) for the
+    // combine; each warp releases the stage after its share of the combine
+    // (the producer refills it only after all NW releases).
+    sync_math();
+    float* ms = reinterpret_cast<float*>(sk);
+    float* ls = ms + NW * GP;
+    float* accs = ls + NW * GP;
+    M::store_state(st, ms, ls, accs);
+    sync_math();
+    {
       T* outp = static_cast<T*>(p.out) + ((int64_t)r.b * p.H + (int64_t)r.h * p.G) * D;
       const bool whole = r.flags & kRecWhole;
+      const bool out8 = (reinterpret_cast<uintptr_t>(outp) & 7u) == 0;
       float* slot = p.partials + (size_t)r.slot * SLOT_FLOATS;
-      for (int idx = tid; idx < GP * D; idx += NW * 32) {
-        const int g = idx / D, d = idx - g * D;
-        float M_ = -INFINITY;
-#pragma unroll
-        for (int ww = 0; ww < NW; ++ww) M_ = fmaxf(M_, ms[ww * GP + g]);
-        float L = 0.f, O = 0.f;
+      // four consecutive dims of one head per thread: the head's NW factors
+      // once, then float4 reads of the warps' accumulators
+      for (int i = tid; i < GP * D / 4; i += NW * 32) {
+        const int g = (4 * i) / D, d = 4 * i - g * D;
+        float mw[NW], M_ = -INFINITY;
 #pragma unroll
         for (int ww = 0; ww < NW; ++ww) {
-          const float mw = ms[ww * GP + g];
-          const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M_);
+          mw[ww] = ms[ww * GP + g];
+          M_ = fmaxf(M_, mw[ww]);
+        }
+        float L = 0.f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int ww = 0; ww < NW; ++ww) {
+          const float f = (mw[ww] == -INFINITY) ? 0.f : exp2f(mw[ww] - M_);
           L = fmaf(ls[ww * GP + g], f, L);
-          O = fmaf(accs[(ww * GP + g) * D + d], f, O);
+          const float4 a = *reinterpret_cast<const float4*>(accs + (ww * GP + g) * D + d);
+          O.x = fmaf(a.x, f, O.x);
+          O.y = fmaf(a.y, f, O.y);
+          O.z = fmaf(a.z, f, O.z);
+          O.w = fmaf(a.w, f, O.w);
         }
         if (whole) {
-          if (g < p.G) outp[g * D + d] = Elem<T>::from_f(O / L);
+          if (g < p.G) {
+            T* o = outp + g * D + d;
+            const T o0 = Elem<T>::from_f(O.x / L), o1 = Elem<T>::from_f(O.y / L);
+            const T o2 = Elem<T>::from_f(O.z / L), o3 = Elem<T>::from_f(O.w / L);
+            if (out8) {
+              const __half2 lo = __halves2half2(o0, o1), hi = __halves2half2(o2, o3);
+              uint2 v;
+              v.x = *reinterpret_cast<const uint32_t*>(&lo);
+              v.y = *reinterpret_cast<const uint32_t*>(&hi);
+              *reinterpret_cast<uint2*>(o) = v;
+            } else {
+              o[0] = o0; o[1] = o1; o[2] = o2; o[3] = o3;
+            }
+          }
         } else {
-          slot[2 * GP + g * D + d] = O;
+          *reinterpret_cast<float4*>(slot + 2 * GP + g * D + d) = O;
           if (d == 0) {
             slot[g] = M_;
             slot[GP + g] = L;
           }
         }
       }
+      fence_proxy_async_smem();  // generic writes to the stage before TMA refills it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
       if (!whole)
         hand_off(PieceHandoff{r.w_first, r.w_last, r.b, r.h, r.pieces, r.first_slot, kHandArrive,
                               0});
-      sync_math();  // ms/ls/accs are free for the next piece
     }
   }
   hand_off(PieceHandoff{0, 0, 0, 0, 0, 0, kHandEnd, 0});

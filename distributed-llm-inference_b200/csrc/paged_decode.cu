@@ -593,6 +593,8 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
     p.counters = reinterpret_cast<unsigned long long*>(wb + ws.counters_off);
     p.partials = reinterpret_cast<float*>(wb + ws.partials_off);
     p.call_tag = next_call_tag();
+    p.q_row = H * D;
+    p.bulk_q = aligned16(q) && (H * D) % 8 == 0;
     CUtensorMap kmap, vmap;
     if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
                     encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
@@ -870,6 +872,8 @@ int pdb_decode_attention_ex(const void* q, const void* k_new, const void* v_new,
                   ((flags & PDB_DECODE_STABLE_POOLS) ? 2 : 0);
   p.q_row = q_row;
   p.kv_row = kv_row;
+  p.bulk_q = aligned16(q) && q_row % 8 == 0 && aligned16(k_new) && aligned16(v_new) &&
+             kv_row % 8 == 0;
   CUtensorMap kmap, vmap;
   if (!(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
         encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
