@@ -728,7 +728,13 @@ int pdb_rope_kv_write(const void* q, const void* k, const void* v, void* q_out, 
       return fail(PDB_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) +
                                          " bytes");
     int32_t* sor = static_cast<int32_t*>(workspace);
-    pdb::valid_scan_kernel<1024, 16><<<1, 1024, 0, st>>>(valid, rows, num_slots, sor);
+    // Programmatic launch: the scan becomes resident while the previous
+    // kernel drains and waits for it (griddepcontrol.wait) before it reads
+    // the mask or overwrites slot_of_row, which that kernel may still read.
+    const cudaError_t le =
+        launch_pdl(pdb::valid_scan_kernel<1024, 16>, dim3(1), dim3(1024), 0, st, valid, rows,
+                   num_slots, sor);
+    if (le != cudaSuccess) return cuda_fail(le, "valid_scan launch");
     slot_of_row = sor;
   }
   pdb::RopeParams p{};
@@ -740,6 +746,7 @@ int pdb_rope_kv_write(const void* q, const void* k, const void* v, void* q_out, 
   p.heads = (int)heads; p.kv_heads = (int)kv_heads; p.dim = (int)head_dim;
   p.num_blocks = num_blocks; p.block_size = (int)block_size;
   p.num_rows = rows;
+  p.after_scan = valid ? 1 : 0;
   return launch_rope(p, dtype, st);
 }
 

@@ -135,6 +135,11 @@ struct RopeParams {
   int64_t table_width;
   int32_t* lengths;
   int advance;
+  // Launched right after valid_scan_kernel (prefill with a valid mask): q, k,
+  // v and positions were complete before the scan started, so the vectorised
+  // kernel rotates q and k and stores q_out / k_out before its dependency
+  // wait, and waits only before the slot writes, which need slot_of_row.
+  int after_scan;
 };
 
 // Position of row r and the element offset of its pool slot (-1: no write).
@@ -302,6 +307,65 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
   }
 }
 
+// Rotate the 16-byte chunk at element j0 of a row's first half and the
+// matching chunk of its second half (rounding as rope_kv_write_kernel).
+// FP16: packed half2 arithmetic. mul/add/sub.rn.f16x2 round the exact
+// result once to FP16, which is what the per-op path does (the fp32 product
+// of two FP16 values is exact, and an fp32 sum of two FP16 values rounds to
+// the same FP16 value as the exact sum), so the results are bit-identical;
+// the products must not be fused with the sum into one fma (one rounding),
+// hence __hmul2_rn (measured: 0 of 4M random pairs differ; with contraction
+// about 1 in 4 did).
+// The rotated chunks are returned in o1 (first half) and o2 (second half).
+template <typename T>
+__device__ __forceinline__ void rope_chunk_pair(const T* in, int j0, int half, const float* cr,
+                                                const float* sr, uint4& o1, uint4& o2);
+
+template <>
+__device__ __forceinline__ void rope_chunk_pair<__half>(const __half* in, int j0, int half,
+                                                        const float* cr, const float* sr,
+                                                        uint4& o1, uint4& o2) {
+  const uint4 a = *reinterpret_cast<const uint4*>(in + j0);
+  const uint4 b = *reinterpret_cast<const uint4*>(in + half + j0);
+  const __half2* x1 = reinterpret_cast<const __half2*>(&a);
+  const __half2* x2 = reinterpret_cast<const __half2*>(&b);
+  __half2* t1 = reinterpret_cast<__half2*>(&o1);
+  __half2* t2 = reinterpret_cast<__half2*>(&o2);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    // cos/sin are FP16 values held as floats: the conversion is exact
+    const __half2 c = __floats2half2_rn(cr[j0 + 2 * e], cr[j0 + 2 * e + 1]);
+    const __half2 s = __floats2half2_rn(sr[j0 + 2 * e], sr[j0 + 2 * e + 1]);
+    // __hmul2_rn: the products are never contracted into an fma with the sum
+    t1[e] = __hsub2(__hmul2_rn(x1[e], c), __hmul2_rn(x2[e], s));
+    t2[e] = __hadd2(__hmul2_rn(x2[e], c), __hmul2_rn(x1[e], s));
+  }
+}
+
+template <>
+__device__ __forceinline__ void rope_chunk_pair<float>(const float* in, int j0, int half,
+                                                       const float* cr, const float* sr,
+                                                       uint4& o1, uint4& o2) {
+  float x1[4], x2[4];
+  Chunk<float>::to_f(*reinterpret_cast<const uint4*>(in + j0), x1);
+  Chunk<float>::to_f(*reinterpret_cast<const uint4*>(in + half + j0), x2);
+  float* t1 = reinterpret_cast<float*>(&o1);
+  float* t2 = reinterpret_cast<float*>(&o2);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float cc = cr[j0 + e], ss = sr[j0 + e];
+    t1[e] = __fsub_rn(__fmul_rn(x1[e], cc), __fmul_rn(x2[e], ss));
+    t2[e] = __fadd_rn(__fmul_rn(x2[e], cc), __fmul_rn(x1[e], ss));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_chunk_pair(T* out, int j0, int half, const uint4& o1,
+                                                 const uint4& o2) {
+  *reinterpret_cast<uint4*>(out + j0) = o1;
+  *reinterpret_cast<uint4*>(out + half + j0) = o2;
+}
+
 // Vectorised variant: 16-byte loads and stores. Requires head_dim*e to be a
 // multiple of 32 bytes (each half a whole number of 16-byte chunks) and
 // 16-byte aligned q/k/v/outputs/pools. ROWS rows per CTA; per row, thread t
@@ -309,7 +373,7 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(RopeParams p) {
 // matching chunks of both halves. Rounding is identical to rope_kv_write_kernel.
 template <typename T, int ROWS>
 __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
-  grid_dependency_wait();  // inputs may come from the previous kernel
+  if (!p.after_scan) grid_dependency_wait();  // inputs may come from the previous kernel
   launch_dependents();     // the attention kernel may start its set-up
   constexpr int VEC = 16 / (int)sizeof(T);
   extern __shared__ float cs[];  // [ROWS][2][dim/2]
@@ -323,7 +387,12 @@ __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
     const int64_t r = r0 + threadIdx.x;
     long long base = -1;
     int64_t pos = 0;
-    if (r < p.num_rows) {
+    if (p.after_scan) {  // the slot is resolved after the dependency wait
+      if (r < p.num_rows) {
+        const int64_t bi = r / p.seq, si = r - bi * p.seq;
+        pos = p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
+      }
+    } else if (r < p.num_rows) {
       int len = 0;
       resolve_row(p, r, &pos, &base, &len);
       if (p.tables && p.advance) p.lengths[r] = len + 1;  // only this thread reads it
@@ -347,6 +416,52 @@ __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
   // Work items per row: q and k chunk pairs (one chunk of each half), then
   // the v row copied as 2*kchunks plain chunks.
   const int qchunks = p.heads * hchunks, kchunks = p.kv_heads * hchunks;
+  if (p.after_scan) {
+    // rotate q and k, store q_out / k_out; then, after the scan, the slots
+    const int rot_row = qchunks + kchunks;
+    for (int i = threadIdx.x; i < ROWS * rot_row; i += blockDim.x) {
+      const int rr = i / rot_row, w = i - rr * rot_row;
+      const int64_t r = r0 + rr;
+      if (r >= p.num_rows) continue;
+      const float* cr = cs + (rr * 2) * half;
+      const float* sr = cr + half;
+      const bool isq = w < qchunks;
+      const int ww = isq ? w : w - qchunks;
+      const int h = ww / hchunks, c = ww - h * hchunks;
+      const int nh = isq ? p.heads : p.kv_heads;
+      const T* in = static_cast<const T*>(isq ? p.q : p.k) + (r * nh + h) * p.dim;
+      T* out = static_cast<T*>(isq ? p.q_out : p.k_out) + (r * nh + h) * p.dim;
+      uint4 o1, o2;
+      rope_chunk_pair<T>(in, c * VEC, half, cr, sr, o1, o2);
+      store_chunk_pair<T>(out, c * VEC, half, o1, o2);
+    }
+    grid_dependency_wait();  // slot_of_row comes from the scan
+    __syncthreads();         // every thread's k_out stores precede the slot copies
+    if (threadIdx.x < ROWS) {
+      const int64_t r = r0 + threadIdx.x;
+      long long base = -1;
+      if (r < p.num_rows) {
+        int64_t pos = 0;
+        int len = 0;
+        resolve_row(p, r, &pos, &base, &len);
+      }
+      slot_base[threadIdx.x] = base;
+    }
+    __syncthreads();
+    // the rotated k row (from k_out) and the v row, each 2*kchunks chunks
+    const int cp_row = 4 * kchunks;
+    for (int i = threadIdx.x; i < ROWS * cp_row; i += blockDim.x) {
+      const int rr = i / cp_row, w = i - rr * cp_row;
+      const int64_t r = r0 + rr;
+      if (r >= p.num_rows || slot_base[rr] < 0) continue;
+      const bool isk = w < 2 * kchunks;
+      const int c = isk ? w : w - 2 * kchunks;
+      const T* src = static_cast<const T*>(isk ? p.k_out : p.v) + r * p.kv_heads * p.dim;
+      T* dst = static_cast<T*>(isk ? p.k_pool : p.v_pool) + slot_base[rr];
+      reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(src)[c];
+    }
+    return;
+  }
   const int per_row = qchunks + kchunks + 2 * kchunks;
   for (int i = threadIdx.x; i < ROWS * per_row; i += blockDim.x) {
     const int rr = i / per_row, w = i - rr * per_row;
@@ -362,29 +477,12 @@ __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
       const T* in = static_cast<const T*>(isq ? p.q : p.k) + (r * nh + h) * p.dim;
       T* out = static_cast<T*>(isq ? p.q_out : p.k_out) + (r * nh + h) * p.dim;
       const int j0 = c * VEC;
-      float x1[VEC], x2[VEC];
-      Chunk<T>::to_f(*reinterpret_cast<const uint4*>(in + j0), x1);
-      Chunk<T>::to_f(*reinterpret_cast<const uint4*>(in + half + j0), x2);
       uint4 o1, o2;
-      T* t1 = reinterpret_cast<T*>(&o1);
-      T* t2 = reinterpret_cast<T*>(&o2);
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const float cc = cr[j0 + e], ss = sr[j0 + e];
-        const T a = Elem<T>::from_f(__fmul_rn(x1[e], cc));
-        const T b = Elem<T>::from_f(__fmul_rn(x2[e], ss));
-        const T d = Elem<T>::from_f(__fmul_rn(x2[e], cc));
-        const T f = Elem<T>::from_f(__fmul_rn(x1[e], ss));
-        t1[e] = Elem<T>::from_f(__fsub_rn(Elem<T>::to_f(a), Elem<T>::to_f(b)));
-        t2[e] = Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(d), Elem<T>::to_f(f)));
-      }
-      *reinterpret_cast<uint4*>(out + j0) = o1;
-      *reinterpret_cast<uint4*>(out + half + j0) = o2;
-      if (!isq && slot_base[rr] >= 0) {
-        T* ks = static_cast<T*>(p.k_pool) + slot_base[rr] + h * p.dim;
-        *reinterpret_cast<uint4*>(ks + j0) = o1;
-        *reinterpret_cast<uint4*>(ks + half + j0) = o2;
-      }
+      rope_chunk_pair<T>(in, j0, half, cr, sr, o1, o2);
+      store_chunk_pair<T>(out, j0, half, o1, o2);
+      if (!isq && slot_base[rr] >= 0)
+        store_chunk_pair<T>(static_cast<T*>(p.k_pool) + slot_base[rr] + h * p.dim, j0, half, o1,
+                            o2);
     } else if (slot_base[rr] >= 0) {
       // v: copy the row's 2*kchunks 16-byte chunks to the slot unchanged
       const int c = w - qchunks - kchunks;  // 0 .. 2*kchunks-1 over the full row
