@@ -325,10 +325,12 @@ __device__ __forceinline__ void fused_piece_start(typename M::State& st, const A
       const int i = 16 * ks + 2 * tg + 8 * r;  // elements i, i + 1 (lower half)
       uint32_t lo = 0u, hi = 0u;
       if (real) {
-        __half l0, h0, l1, h1;
-        rot(__low2float(qx1[ks][r]), __low2float(qx2[ks][r]), i, &l0, &h0);
-        rot(__high2float(qx1[ks][r]), __high2float(qx2[ks][r]), i + 1, &l1, &h1);
-        const __half2 lo2 = __halves2half2(l0, l1), hi2 = __halves2half2(h0, h1);
+        // the same rounding as rot(), two elements at a time: each product
+        // and the sum rounded once to FP16 (no fma contraction)
+        const __half2 c = __floats2half2_rn(cs[i], cs[i + 1]);
+        const __half2 sn = __floats2half2_rn(cs[HALF + i], cs[HALF + i + 1]);
+        const __half2 lo2 = __hsub2(__hmul2_rn(qx1[ks][r], c), __hmul2_rn(qx2[ks][r], sn));
+        const __half2 hi2 = __hadd2(__hmul2_rn(qx2[ks][r], c), __hmul2_rn(qx1[ks][r], sn));
         lo = *reinterpret_cast<const uint32_t*>(&lo2);
         hi = *reinterpret_cast<const uint32_t*>(&hi2);
       }
