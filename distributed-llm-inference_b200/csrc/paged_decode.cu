@@ -470,6 +470,19 @@ int launch_rope(const pdb::RopeParams& p, int dtype, cudaStream_t st) {
       constexpr int kRows = decltype(rows_tag)::value;
       const unsigned grid = (unsigned)((p.num_rows + kRows - 1) / kRows);
       const size_t smem = (size_t)kRows * p.dim * sizeof(float);
+      // prefill after the scan: rows staged in shared memory (within the
+      // default 48 KB of dynamic shared memory; larger rows take the kernel
+      // that reads them from global memory)
+      const size_t staged = smem + (size_t)kRows * (p.heads + 2 * p.kv_heads) * p.dim * esize;
+      if (p.after_scan && staged <= 48 * 1024) {
+        if (dtype == PDB_DTYPE_FLOAT16)
+          launch_pdl(pdb::rope_prefill_vec_kernel<__half, kRows>, dim3(grid), dim3(256), staged,
+                     st, p);
+        else
+          launch_pdl(pdb::rope_prefill_vec_kernel<float, kRows>, dim3(grid), dim3(256), staged,
+                     st, p);
+        return;
+      }
       if (dtype == PDB_DTYPE_FLOAT16)
         launch_pdl(pdb::rope_kv_write_vec_kernel<__half, kRows>, dim3(grid), dim3(256), smem, st, p);
       else
