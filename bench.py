@@ -483,11 +483,15 @@ def run_ours(args):
     peak = peak or 6650.0
     achieved = attn_bytes / (ms_attn * 1e-3) / 1e9
     traffic = None
+    # DRAM traffic of the dominant launch: the ncu traffic / algorithmic-bytes
+    # ratio of a smaller capture of the same kernel and workload (the full
+    # launch is too large for a multi-pass capture; traffic grows with the
+    # K/V bytes read), applied to this rank's algorithmic bytes per launch.
     tf = REPO / "profiles" / "traffic_attn_tma_llama3_b256.json"
-    if tf.exists():
+    if tf.exists() and step.fused:
         tj = json.loads(tf.read_text())
-        if tj.get("workload") == full.name and tj.get("world") == world:
-            traffic = tj.get("bytes_per_launch")
+        if tj.get("workload") == full.name and tj.get("ratio_to_algorithmic"):
+            traffic = int(round(tj["ratio_to_algorithmic"] * attn_bytes))
 
     e2e = None
     if not args.no_e2e:

@@ -475,12 +475,21 @@ int launch_rope(const pdb::RopeParams& p, int dtype, cudaStream_t st) {
       // that reads them from global memory)
       const size_t staged = smem + (size_t)kRows * (p.heads + 2 * p.kv_heads) * p.dim * esize;
       if (p.after_scan && staged <= 48 * 1024) {
-        if (dtype == PDB_DTYPE_FLOAT16)
-          launch_pdl(pdb::rope_prefill_vec_kernel<__half, kRows>, dim3(grid), dim3(256), staged,
-                     st, p);
-        else
+        if (dtype == PDB_DTYPE_FLOAT16) {
+          // compile-time shapes for the SmolLM2 and Llama-3-8B heads
+          if (p.heads == 9 && p.kv_heads == 3 && p.dim == 64)
+            launch_pdl(pdb::rope_prefill_vec_kernel<__half, kRows, 9, 3, 64>, dim3(grid),
+                       dim3(256), staged, st, p);
+          else if (p.heads == 32 && p.kv_heads == 8 && p.dim == 128)
+            launch_pdl(pdb::rope_prefill_vec_kernel<__half, kRows, 32, 8, 128>, dim3(grid),
+                       dim3(256), staged, st, p);
+          else
+            launch_pdl(pdb::rope_prefill_vec_kernel<__half, kRows>, dim3(grid), dim3(256),
+                       staged, st, p);
+        } else {
           launch_pdl(pdb::rope_prefill_vec_kernel<float, kRows>, dim3(grid), dim3(256), staged,
                      st, p);
+        }
         return;
       }
       if (dtype == PDB_DTYPE_FLOAT16)

@@ -501,7 +501,10 @@ __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
 // so it runs before the dependency wait; after it, each row's slot is
 // resolved and the rotated k and the v row are copied to it from shared
 // memory.
-template <typename T, int ROWS>
+// HQ, HK, DIM: the head counts and head_dim as compile-time constants for
+// the common shapes (0: taken from p), which turns the index arithmetic's
+// divisions into multiplications.
+template <typename T, int ROWS, int HQ = 0, int HK = 0, int DIM = 0>
 __global__ void __launch_bounds__(256) rope_prefill_vec_kernel(RopeParams p) {
   launch_dependents();
   constexpr int VEC = 16 / (int)sizeof(T);
@@ -509,10 +512,12 @@ __global__ void __launch_bounds__(256) rope_prefill_vec_kernel(RopeParams p) {
   __shared__ long long slot_base[ROWS];
   __shared__ float row_fpos[ROWS];
   const int tid = threadIdx.x;
-  const int half = p.dim >> 1, hchunks = half / VEC;
-  const int qc = p.heads * p.dim / VEC, kc = p.kv_heads * p.dim / VEC;  // chunks per q / k row
+  const int heads = HQ ? HQ : p.heads, kv_heads = HK ? HK : p.kv_heads;
+  const int dim = DIM ? DIM : p.dim;
+  const int half = dim >> 1, hchunks = half / VEC;
+  const int qc = heads * dim / VEC, kc = kv_heads * dim / VEC;  // chunks per q / k row
   const int row_chunks = qc + 2 * kc;                                    // q, k, v
-  uint4* stg = reinterpret_cast<uint4*>(cs + ROWS * p.dim);             // [ROWS][row_chunks]
+  uint4* stg = reinterpret_cast<uint4*>(cs + ROWS * dim);               // [ROWS][row_chunks]
   const int64_t r0 = (int64_t)blockIdx.x * ROWS;
   const int nrows = p.num_rows - r0 < ROWS ? (int)(p.num_rows - r0) : ROWS;
   for (int i = tid; i < nrows * row_chunks; i += blockDim.x) {
@@ -539,16 +544,16 @@ __global__ void __launch_bounds__(256) rope_prefill_vec_kernel(RopeParams p) {
   }
   cp_async_wait<0>();
   __syncthreads();
-  const int qpairs = p.heads * hchunks, rot_row = qpairs + p.kv_heads * hchunks;
+  const int qpairs = heads * hchunks, rot_row = qpairs + kv_heads * hchunks;
   for (int i = tid; i < nrows * rot_row; i += blockDim.x) {
     const int rr = i / rot_row, w = i - rr * rot_row;
     const int64_t r = r0 + rr;
     const bool isq = w < qpairs;
     const int ww = isq ? w : w - qpairs;
     const int h = ww / hchunks, c = ww - h * hchunks;
-    T* in = reinterpret_cast<T*>(stg + (size_t)rr * row_chunks + (isq ? 0 : qc)) + h * p.dim;
-    T* out = isq ? static_cast<T*>(p.q_out) + (r * p.heads + h) * p.dim
-                 : static_cast<T*>(p.k_out) + (r * p.kv_heads + h) * p.dim;
+    T* in = reinterpret_cast<T*>(stg + (size_t)rr * row_chunks + (isq ? 0 : qc)) + h * dim;
+    T* out = isq ? static_cast<T*>(p.q_out) + (r * heads + h) * dim
+                 : static_cast<T*>(p.k_out) + (r * kv_heads + h) * dim;
     uint4 o1, o2;
     rope_chunk_pair<T>(in, c * VEC, half, cs + (rr * 2) * half, cs + (rr * 2 + 1) * half, o1, o2);
     store_chunk_pair<T>(out, c * VEC, half, o1, o2);
