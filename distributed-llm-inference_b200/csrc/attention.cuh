@@ -381,6 +381,7 @@ struct MmaMath {
   static_assert(SUB_ == 1 || LAYOUT_ == kTma128B, "multi-block tiles are staged by TMA");
   static constexpr int NW = 4, NT = 128;
   static constexpr int WT = 16 * SUB;    // tokens per warp per tile (SUB x MMA M)
+  static constexpr int CHUNKS = D / 8;   // 16-byte chunks of a K/V row
   static constexpr int TILE = NW * WT;   // 64 * SUB tokens
   static constexpr int TILE_UNITS = TILE / kUnitTokens;
   static constexpr bool SWZ = true;
@@ -564,10 +565,14 @@ struct MmaMath {
 // ===========================================================================
 // Inner loop 2: SIMT fp32 FMA (FP32, and FP16 shapes outside MmaMath)
 // ===========================================================================
-template <typename T_, int D_, int GP_, int TPG_, int STAGES_>
+template <typename T_, int D_, int GP_, int TPG_, int STAGES_, int LAYOUT_ = kRowSwizzle>
 struct SimtMath {
   using T = T_;
   static constexpr int D = D_;
+  // kRowSwizzle here: plain row-major stage tiles (cp.async); kTma128B: the
+  // stage layout of the TMA kernels (128-byte column blocks, chunks XORed with
+  // the row).
+  static constexpr int LAYOUT = LAYOUT_;
   static constexpr int GP = GP_;          // group size padded to a power of 2
   static constexpr int TPG = TPG_;        // tokens per lane group per tile
   static constexpr int STAGES = STAGES_;  // cp.async ring depth
@@ -580,6 +585,7 @@ struct SimtMath {
   static constexpr int TPW = 32 / LPT;         // lane groups per warp
   static constexpr int NW = 4, NT = 128;
   static constexpr int TW = TPW * TPG;      // tokens per warp per tile
+  static constexpr int WT = TW;
   static constexpr int TILE = NW * TW;      // tokens per tile
   static constexpr int TILE_UNITS = TILE / kUnitTokens;
   static constexpr int DPL = D / 32;        // dims per lane (PV)
@@ -591,6 +597,23 @@ struct SimtMath {
   static_assert(TILE % kUnitTokens == 0, "tile must hold whole units");
   static_assert(D % 32 == 0 && CH % LPT == 0, "unsupported head_dim");
   static_assert(DPL * E <= 16, "PV lane width");
+  static constexpr int CHUNKS = CH;  // 16-byte chunks of a K/V row
+  static_assert(LAYOUT_ != kTma128B || (D * E) % 128 == 0, "whole 128-byte column blocks");
+
+  // Byte offset of element d of token row `row` in a stage tile.
+  __device__ static __forceinline__ int elem_offset(int row, int d) {
+    if constexpr (LAYOUT == kTma128B) {
+      const int chunk = d / VEC;
+      return (chunk >> 3) * (TILE * 128) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4) +
+             (d % VEC) * E;
+    } else {
+      return (row * D + d) * E;
+    }
+  }
+  // Byte offset of 16-byte chunk `col` of token row `row`.
+  __device__ static __forceinline__ int offset(int row, int col) {
+    return elem_offset(row, col * VEC);
+  }
 
   struct State {
     float q[GP][DL];
@@ -619,12 +642,33 @@ struct SimtMath {
     }
   }
 
+  // begin_piece with the group's G query rows (D elements each, consecutive)
+  // at `qbase`, in global or shared memory.
+  __device__ static void begin_piece_at(State& s, const T* qbase, int G) {
+    const int l8 = (threadIdx.x & 31) % LPT;
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        if (g < G) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(qbase + g * D + (l8 + LPT * c) * VEC);
+          Chunk<T>::to_f(raw, &s.q[g][c * VEC]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) s.q[g][c * VEC + e] = 0.f;
+        }
+      }
+      s.m[g] = -INFINITY;
+      s.l[g] = 0.f;
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) s.acc[g][d] = 0.f;
+    }
+  }
+
   __device__ static void compute_tile(State& st, const AttnParams& p, const unsigned char* skb,
                                       const unsigned char* svb, int ntok, float* ps) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = lane / LPT, l8 = lane % LPT;
-    const T* sk = reinterpret_cast<const T*>(skb);
-    const T* sv = reinterpret_cast<const T*>(svb);
     float s[GP][TPG];
 #pragma unroll
     for (int r = 0; r < TPG; ++r) {
@@ -635,7 +679,7 @@ struct SimtMath {
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {
         float kf[VEC];
-        lds_to_f<T, VEC>(sk + row * D + (l8 + LPT * c) * VEC, kf);
+        lds_to_f<T, VEC>(reinterpret_cast<const T*>(skb + offset(row, l8 + LPT * c)), kf);
 #pragma unroll
         for (int g = 0; g < GP; ++g)
 #pragma unroll
@@ -691,7 +735,8 @@ struct SimtMath {
 #pragma unroll
         for (int g = 0; g < GP; ++g) pv[g] = pw[i * GP + g];
         float vf[DPL];
-        lds_to_f<T, DPL>(sv + (warp * TW + i) * D + lane * DPL, vf);
+        lds_to_f<T, DPL>(reinterpret_cast<const T*>(svb + elem_offset(warp * TW + i, lane * DPL)),
+                         vf);
 #pragma unroll
         for (int g = 0; g < GP; ++g)
 #pragma unroll

@@ -360,19 +360,24 @@ __device__ __forceinline__ void fused_piece_start(typename M::State& st, const A
 template <class M>
 struct DynStreamK {
   static_assert(M::LAYOUT == kTma128B, "dynamic kernel stages with TMA");
+  using T = typename M::T;
+  static constexpr int E = (int)sizeof(T);
   static constexpr int D = M::D, GP = M::GP, NW = M::NW, STAGES = M::STAGES;
   static constexpr int NT = (NW + 2) * 32;  // math warps, producer, epilogue
-  static constexpr int HALVES = D / 64;
-  static constexpr int UNIT_BYTES = 2 * kUnitTokens * D * 2;
-  // Per-stage prefetch slots: a piece's q rows (G <= GP rows of D halves)
+  static constexpr int BOX_COLS = 128 / E;  // elements of a 128-byte TMA box row
+  static constexpr int HALVES = D / BOX_COLS;  // 128-byte column blocks of a row
+  static constexpr int UNIT_BYTES = 2 * kUnitTokens * D * E;
+  // Per-stage prefetch slots: a piece's q rows (G <= GP rows of D elements)
   // and the new token's k and v rows.
-  static constexpr int QPRE_BYTES = GP * D * 2;
-  static constexpr int KVPRE_BYTES = 2 * D * 2;
+  static constexpr int QPRE_BYTES = GP * D * E;
+  static constexpr int KVPRE_BYTES = 2 * D * E;
+  // SIMT inner loops' probability broadcast (0 for the tensor-core loop)
+  static constexpr int EXTRA_BYTES = M::EXTRA_FLOATS * 4;
   // At a piece end the warps' partial states (m, l, O per head) go through
   // the buffer of the stage just consumed.
   static_assert(NW * GP * (D + 2) * 4 <= M::STAGE_BYTES, "merge area fits in a stage");
   static size_t smem_bytes(int B) {
-    return 1024 + (size_t)STAGES * (M::STAGE_BYTES + QPRE_BYTES + KVPRE_BYTES) +
+    return 1024 + (size_t)STAGES * (M::STAGE_BYTES + QPRE_BYTES + KVPRE_BYTES) + EXTRA_BYTES +
            (size_t)(4 * B + 1 + kDynMisc) * 4 + (2 * STAGES + 2 * kHandoffDepth) * 8 + 16 +
            (size_t)STAGES * sizeof(TileRecord) + kHandoffDepth * sizeof(PieceHandoff) +
            (size_t)D * 4 + (size_t)2 * D * 2 + (size_t)D / 2 * 4 +
@@ -399,7 +404,8 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* qpre = smem + (size_t)STAGES * M::STAGE_BYTES;  // [STAGES][QPRE_BYTES]
   unsigned char* kvpre = qpre + (size_t)STAGES * K::QPRE_BYTES;  // [STAGES][KVPRE_BYTES]
-  int* P = reinterpret_cast<int*>(kvpre + (size_t)STAGES * K::KVPRE_BYTES);  // by stream position
+  float* extra = reinterpret_cast<float*>(kvpre + (size_t)STAGES * K::KVPRE_BYTES);
+  int* P = reinterpret_cast<int*>(extra + M::EXTRA_FLOATS);  // by stream position
   int* Ls = P + p.B + 1;
   int* ord = Ls + p.B;
   int* Lidx = ord + p.B;  // lengths by sequence index (plan only)
@@ -575,7 +581,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
         const bool qp = p.bulk_q != 0 && waited && piece_first;
         const bool kvp = qp && new_tok;
         if (lane == 0) {
-          const int qbytes = p.G * D * 2;
+          const int qbytes = p.G * D * K::E;
           if (qp) recs[s].flags |= kRecQPre;
           fence_proxy_async_smem();
           mbar_arrive_expect_tx(&full[s], (uint32_t)__popc(okmask) * K::UNIT_BYTES +
@@ -583,7 +589,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
           const int bq = ord[c.b];
           if (qp)
             bulk_load(qpre + (size_t)s * K::QPRE_BYTES,
-                      static_cast<const __half*>(p.q) + (int64_t)bq * p.q_row +
+                      static_cast<const T*>(p.q) + (int64_t)bq * p.q_row +
                           (int64_t)c.h * p.G * D,
                       (uint32_t)qbytes, &full[s]);
           if (kvp) {
@@ -600,8 +606,8 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
 #pragma unroll
           for (int hf = 0; hf < K::HALVES; ++hf) {
             const int dst = hf * (TILE * 128) + lane * kUnitTokens * 128;
-            tma_load_3d(sk + dst, &kmap, hf * 64, c.h, row0, &full[s]);
-            tma_load_3d(sv + dst, &vmap, hf * 64, c.h, row0, &full[s]);
+            tma_load_3d(sk + dst, &kmap, hf * K::BOX_COLS, c.h, row0, &full[s]);
+            tma_load_3d(sv + dst, &vmap, hf * K::BOX_COLS, c.h, row0, &full[s]);
           }
         }
         ++k;
@@ -685,9 +691,9 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
     unsigned char* sv = sk + M::TILE_BYTES;
     const int r0 = warp * M::WT;
     const bool pre = (r.flags & kRecQPre) != 0;
-    const __half* qbase =
-        pre ? reinterpret_cast<const __half*>(qpre + (size_t)s * K::QPRE_BYTES)
-            : static_cast<const __half*>(p.q) + (int64_t)r.b * p.q_row + (int64_t)r.h * p.G * D;
+    const T* qbase =
+        pre ? reinterpret_cast<const T*>(qpre + (size_t)s * K::QPRE_BYTES)
+            : static_cast<const T*>(p.q) + (int64_t)r.b * p.q_row + (int64_t)r.h * p.G * D;
     if constexpr (FUSE) {
       if (r.flags & kRecFirst) {
         const __half* kvs = reinterpret_cast<const __half*>(kvpre + (size_t)s * K::KVPRE_BYTES);
@@ -721,8 +727,8 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
       }
     }
     if (r0 < r.ntok && r0 + M::WT > r.ntok) {
-      for (int i = lane; i < (r0 + M::WT - r.ntok) * (D / 8); i += 32) {
-        const int row = r.ntok + i / (D / 8), col = i % (D / 8);
+      for (int i = lane; i < (r0 + M::WT - r.ntok) * M::CHUNKS; i += 32) {
+        const int row = r.ntok + i / M::CHUNKS, col = i % M::CHUNKS;
         *reinterpret_cast<uint4*>(sv + M::offset(row, col)) = make_uint4(0, 0, 0, 0);
       }
       fence_proxy_async_smem();
@@ -733,7 +739,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
     if (r.flags & kRecFirst) {
       if constexpr (!FUSE) M::begin_piece_at(st, qbase, p.G);  // fused: done above
     }
-    M::compute_tile(st, p, sk, sv, r.ntok, nullptr);
+    M::compute_tile(st, p, sk, sv, r.ntok, extra);
     if (!(r.flags & kRecLast)) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -753,6 +759,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
       T* outp = static_cast<T*>(p.out) + ((int64_t)r.b * p.H + (int64_t)r.h * p.G) * D;
       const bool whole = r.flags & kRecWhole;
       const bool out8 = (reinterpret_cast<uintptr_t>(outp) & 7u) == 0;
+      const bool out16 = (reinterpret_cast<uintptr_t>(outp) & 15u) == 0;
       float* slot = p.partials + (size_t)r.slot * SLOT_FLOATS;
       // four consecutive dims of one head per thread: the head's NW factors
       // once, then float4 reads of the warps' accumulators
@@ -781,18 +788,35 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
             T* o = outp + g * D + d;
             const T o0 = Elem<T>::from_f(O.x / L), o1 = Elem<T>::from_f(O.y / L);
             const T o2 = Elem<T>::from_f(O.z / L), o3 = Elem<T>::from_f(O.w / L);
-            if (out8) {
-              const __half2 lo = __halves2half2(o0, o1), hi = __halves2half2(o2, o3);
-              uint2 v;
-              v.x = *reinterpret_cast<const uint32_t*>(&lo);
-              v.y = *reinterpret_cast<const uint32_t*>(&hi);
-              *reinterpret_cast<uint2*>(o) = v;
+            if constexpr (sizeof(T) == 2) {
+              if (out8) {
+                const __half2 lo = __halves2half2(o0, o1), hi = __halves2half2(o2, o3);
+                uint2 v;
+                v.x = *reinterpret_cast<const uint32_t*>(&lo);
+                v.y = *reinterpret_cast<const uint32_t*>(&hi);
+                *reinterpret_cast<uint2*>(o) = v;
+              } else {
+                o[0] = o0; o[1] = o1; o[2] = o2; o[3] = o3;
+              }
             } else {
-              o[0] = o0; o[1] = o1; o[2] = o2; o[3] = o3;
+              if (out16) {
+                *reinterpret_cast<float4*>(o) = make_float4(o0, o1, o2, o3);
+              } else {
+                o[0] = o0; o[1] = o1; o[2] = o2; o[3] = o3;
+              }
             }
           }
         } else {
-          *reinterpret_cast<float4*>(slot + 2 * GP + g * D + d) = O;
+          // 16-byte stores when every slot and its O block start 16-byte
+          // aligned (GP even); GP 1 (the SIMT inner loop's MHA case) stores
+          // the four floats one by one
+          constexpr bool kSlotVec = (GP * (D + 2) * 4) % 16 == 0 && (2 * GP * 4) % 16 == 0;
+          float* so = slot + 2 * GP + g * D + d;
+          if constexpr (kSlotVec) {
+            *reinterpret_cast<float4*>(so) = O;
+          } else {
+            so[0] = O.x; so[1] = O.y; so[2] = O.z; so[3] = O.w;
+          }
           if (d == 0) {
             slot[g] = M_;
             slot[GP + g] = L;

@@ -201,17 +201,19 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// Pool [N, bs, KVH, D] (FP16) viewed as [N*bs rows, KVH, D]; box = one
-// 16-token unit of one kv head, 64 columns, 128-byte swizzle.
+// Pool [N, bs, KVH, D] (FP16, or FP32 with esize 4) viewed as
+// [N*bs rows, KVH, D]; box = one 16-token unit of one kv head, 128 bytes of
+// columns (64 FP16 / 32 FP32 elements), 128-byte swizzle.
 bool encode_pool_map(CUtensorMap* m, const void* pool, int64_t N, int64_t bs, int64_t KVH,
-                     int64_t D) {
+                     int64_t D, int esize = 2) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
   const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)KVH, (cuuint64_t)(N * bs)};
-  const cuuint64_t strides[2] = {(cuuint64_t)(D * 2), (cuuint64_t)(KVH * D * 2)};
-  const cuuint32_t box[3] = {64, 1, (cuuint32_t)pdb::kUnitTokens};
+  const cuuint64_t strides[2] = {(cuuint64_t)(D * esize), (cuuint64_t)(KVH * D * esize)};
+  const cuuint32_t box[3] = {(cuuint32_t)(128 / esize), 1, (cuuint32_t)pdb::kUnitTokens};
   const cuuint32_t estr[3] = {1, 1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(pool), dims, strides, box,
+  return enc(m, esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+             const_cast<void*>(pool), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -262,6 +264,32 @@ bool pick_simt(int D, int G, FastKernel* out) {
     case 32: return pick_simt_gp<T, 32>(G, out);
     case 64: return pick_simt_gp<T, 64>(G, out);
     case 128: return pick_simt_gp<T, 128>(G, out);
+    default: return false;
+  }
+}
+
+// FP32: the SIMT inner loop in the TMA producer / dynamic-tail kernel
+// (block_size % 16 == 0); 32-token tiles, ~96 KB of stages so that two CTAs
+// stay resident per SM.
+template <int D, int GP>
+FastKernel dyn_simt_f32() {
+  if constexpr (D == 128) return make_dyn<pdb::SimtMath<float, D, GP, 2, 3, pdb::kTma128B>>();
+  else return make_dyn<pdb::SimtMath<float, D, GP, 2, 6, pdb::kTma128B>>();
+}
+template <int D>
+bool pick_dyn_f32_gp(int G, FastKernel* out) {
+  if (G <= 1) { *out = dyn_simt_f32<D, 1>(); return true; }
+  if (G <= 2) { *out = dyn_simt_f32<D, 2>(); return true; }
+  if (G <= 4) { *out = dyn_simt_f32<D, 4>(); return true; }
+  if constexpr (D <= 64) {
+    if (G <= 8) { *out = dyn_simt_f32<D, 8>(); return true; }
+  }
+  return false;
+}
+bool pick_dyn_f32(int D, int G, FastKernel* out) {
+  switch (D) {
+    case 64: return pick_dyn_f32_gp<64>(G, out);
+    case 128: return pick_dyn_f32_gp<128>(G, out);
     default: return false;
   }
 }
@@ -360,6 +388,7 @@ bool fast_applicable(int64_t B, int64_t H, int64_t KVH, int64_t D, int dtype, Fa
     return pick_simt<__half>((int)D, G, k);
   }
   if (family == kCpAsyncMma || family == kStaticTma) return false;
+  if (family == kAny && tma_ok && pick_dyn_f32((int)D, G, k)) return true;
   return pick_simt<float>((int)D, G, k);
 }
 
@@ -542,8 +571,9 @@ size_t pdb_paged_attention_workspace_size(int64_t batch, int64_t heads, int64_t 
     if (tensor_map_encoder() && pick_tma((int)head_dim, G, &cand[n])) ++n;
     if (pick_mma((int)head_dim, G, &cand[n])) ++n;
     if (pick_simt<__half>((int)head_dim, G, &cand[n])) ++n;
-  } else if (pick_simt<float>((int)head_dim, G, &cand[n])) {
-    ++n;
+  } else {
+    if (tensor_map_encoder() && pick_dyn_f32((int)head_dim, G, &cand[n])) ++n;
+    if (pick_simt<float>((int)head_dim, G, &cand[n])) ++n;
   }
   for (int i = 0; i < n; ++i) {
     const int64_t grid = fast_grid(dev, cand[i], batch, kv_heads, max_length);
@@ -618,8 +648,9 @@ int pdb_paged_attention_impl(const void* q, const void* k_pool, const void* v_po
     p.q_row = H * D;
     p.bulk_q = aligned16(q) && (H * D) % 8 == 0;
     CUtensorMap kmap, vmap;
-    if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
-                    encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
+    const int esize = dtype == PDB_DTYPE_FLOAT32 ? 4 : 2;
+    if (fk.tma && !(encode_pool_map(&kmap, k_pool, N, bs, KVH, D, esize) &&
+                    encode_pool_map(&vmap, v_pool, N, bs, KVH, D, esize)))
       return fail(PDB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV pools");
     fk.launch(p, (int)grid, fk.smem((int)B), st, &kmap, &vmap);
   } else {
