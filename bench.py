@@ -1175,7 +1175,8 @@ def measure_prefill_write(device, steps: int, warmup: int, impl: str = "ours") -
                                   d["physical"], d["offsets"], d["positions"], d["inv_freq"],
                                   valid=d["valid"], q_out=q_o, k_out=k_o)
             return step
-        which = "rope_kv_write_vec_kernel + valid_scan_kernel (varlen scatter into the pages)"
+        which = ("valid_scan_kernel + rope_prefill_vec_kernel (rows staged in shared memory, "
+                 "varlen scatter into the pages)")
     stream = torch.cuda.Stream(device)
     g = _graph_of_steps([make(d) for d in copies], steps, stream, device, warmup)
     ms, clk, reps = timed_replays(g.replay, stream, device, steps)
