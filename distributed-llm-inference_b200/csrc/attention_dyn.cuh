@@ -13,7 +13,12 @@
 //     a time with a tagged atomic counter once their static range is done.
 // Tail fraction and chunk size were chosen by measurement on B200 (Llama-3-8B
 // shape, batch 32 to 256): smaller chunks or a larger tail cost more in piece
-// finishes and merges than they gain in balance.
+// finishes and merges than they gain in balance. A call whose static shares
+// would be short (under kTailMinTiles tiles per CTA) has no tail: there a
+// claimed chunk (a piece start, four tiles at the rate of one CTA, an
+// arrival) finishes after the unclaimed CTAs, so the tail made the stragglers
+// it was meant to absorb (Llama-3-8B shape at 32 sequences: 39.7 -> 36.3 us
+// per launch without it; 64 sequences and up keep it).
 // The unit stream lists first the sequences whose per-head segments are
 // longer than two tail chunks, then the others (each group in index order),
 // so the tail holds short segments that few chunk boundaries cut and the
@@ -44,6 +49,7 @@ namespace pdb {
 constexpr int kTailDen = 16;         // tail = U / kTailDen units
 constexpr int kTailChunksPerCta = 4;  // target tail chunks per launched CTA
 constexpr int kMinChunkTiles = 4;     // a tail chunk covers at least this many tiles
+constexpr int kTailMinTiles = 24;     // no tail below this many tiles per launched CTA
 
 // Worker layout of one call: static workers 0..gs-1 over [0, Us), tail
 // workers gs..gs+K-1 over [Us, U).
@@ -66,7 +72,7 @@ __host__ __device__ __forceinline__ DynPlan make_dyn_plan(int64_t U, int64_t lau
                                                           int tile_units) {
   DynPlan pl;
   pl.U = U;
-  int64_t Ut = (U >= 8 * launched * tile_units) ? U / kTailDen : 0;
+  int64_t Ut = (U >= (int64_t)kTailMinTiles * launched * tile_units) ? U / kTailDen : 0;
   int64_t K = launched * kTailChunksPerCta;
   const int64_t kmax = Ut / ((int64_t)kMinChunkTiles * tile_units);
   if (K > kmax) K = kmax;

@@ -149,7 +149,7 @@ def test_install_rebinds_module_global(pkg):
 
 
 @pytest.mark.parametrize("units,launched", [(1, 296), (15, 296), (16, 296), (2048, 296),
-                                            (9471, 296), (9472, 296), (40000, 296),
+                                            (9472, 296), (28415, 296), (28416, 296), (40000, 296),
                                             (163000, 296), (20000, 148), (7, 1), (100000, 1)])
 def test_dynamic_partition_covers_units(lib, units, launched):
     """Static ranges + tail chunks partition [0, units) into non-empty,
