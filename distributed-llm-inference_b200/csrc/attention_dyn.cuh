@@ -281,12 +281,17 @@ constexpr int kDynMisc = 32;  // ints of per-CTA scratch
 // token is patched and the pool slot written. Per-op FP16 rounding as in
 // rope_kv_write. `qbase` points at the group's G query rows, `knew` / `vnew`
 // at the token's k and v rows. `sync` is a barrier over the math threads.
+// `cs_pos` is the position the table in `cs` was built for: consecutive
+// pieces of one sequence (its kv heads are adjacent in the unit stream) share
+// the position, and the table is reused (every math thread holds the same
+// cs_pos, so all skip the build and its barrier together; the previous
+// piece's reads of the table ended before its last tile's combine).
 template <class M, class Sync>
 __device__ __forceinline__ void fused_piece_start(typename M::State& st, const AttnParams& p,
                                                   const __half* qbase, const __half* knew,
                                                   const __half* vnew, int pos, bool new_tok,
                                                   const float* invf, float* cs, __half* newrow,
-                                                  Sync sync) {
+                                                  int& cs_pos, Sync sync) {
   constexpr int D = M::D, KS = M::KSTEPS, HALF = D / 2;
   static_assert(KS % 2 == 0, "lower and upper halves in whole k-steps");
   const int tid = threadIdx.x, lane = tid & 31, g = lane >> 2, tg = lane & 3;
@@ -308,13 +313,16 @@ __device__ __forceinline__ void fused_piece_start(typename M::State& st, const A
     v1 = vnew[tid];
     v2 = vnew[tid + HALF];
   }
-  if (tid < HALF) {
-    float c, s;
-    rope_cos_sin<__half>(__fmul_rn((float)pos, invf[tid]), &c, &s);
-    cs[tid] = __half2float(__float2half_rn(c));
-    cs[HALF + tid] = __half2float(__float2half_rn(s));
+  if (pos != cs_pos) {
+    if (tid < HALF) {
+      float c, s;
+      rope_cos_sin<__half>(__fmul_rn((float)pos, invf[tid]), &c, &s);
+      cs[tid] = __half2float(__float2half_rn(c));
+      cs[HALF + tid] = __half2float(__float2half_rn(s));
+    }
+    cs_pos = pos;
+    sync();
   }
-  sync();
   auto rot = [&](float x1, float x2, int i, __half* o1, __half* o2) {
     const float c = cs[i], sn = cs[HALF + i];
     const float a = __half2float(__float2half_rn(__fmul_rn(x1, c)));
@@ -671,6 +679,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
 
   // ---------------- math warps ----------------
   typename M::State st;
+  int cs_pos = -1;  // position of the fused prologue's cos/sin table (none yet)
   auto sync_math = [] { named_bar_sync(1, NW * 32); };
   int hk = 0;  // pieces handed to the epilogue warp
   // Queue entry hk % depth: warp 0 waits until the epilogue warp has taken
@@ -707,7 +716,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
         fused_piece_start<M>(st, p, qbase, pre ? kvs : static_cast<const __half*>(p.k_new) + kvo,
                              pre ? kvs + D : static_cast<const __half*>(p.v_new) + kvo,
                              r.len - 1, (r.flags & kRecNewTok) != 0, invf, cs_tab, newrow,
-                             sync_math);
+                             cs_pos, sync_math);
       }
       // The new token's row of this tile: the TMA brought the slot's old
       // bytes; the owning warp writes the rotated k and the v in their place
