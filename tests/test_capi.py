@@ -168,6 +168,9 @@ def test_dynamic_partition_covers_units(lib, units, launched):
     if len(tail):
         assert np.all(tail[:, 1] - tail[:, 0] >= 16)  # four 64-token tiles
         assert tail[0, 0] == units - units // 16
+    # short static shares (under 24 tiles of 4 units per launched CTA) get no tail
+    if units < 24 * 4 * launched:
+        assert len(tail) == 0
 
 
 def test_prefill_and_decode_selector_checks(lib):
