@@ -278,51 +278,79 @@ def e2e_run(w, t, steps, warmup, device):
     slots for the two-launch path) from pinned host memory, runs
     decode_attention (or rope_kv_write + paged_attention where the fused
     kernel does not apply), and copies each layer's attention output back to
-    pinned host memory. Copies move in groups of 4 layers on separate copy
-    streams: a group's inputs are copied while the previous group computes
-    and its outputs while the next one computes (event ordering)."""
+    pinned host memory. Layers move in groups: a group's inputs sit side by
+    side in one pinned buffer and arrive with one copy, while the previous
+    group computes; its outputs leave with one copy while the next group
+    computes (separate copy streams, event ordering). The first and the last
+    group hold one layer, so little copy time is left outside the compute."""
     L = w.layers
     fused = PKG.decode_attention_supported(t.q[0], t.k_pools[0])
-    pin = lambda x: x.cpu().pin_memory()  # noqa: E731
-    h_q = [pin(x) for x in t.q]
-    h_k = [pin(x) for x in t.k]
-    h_v = [pin(x) for x in t.v]
     meta = (t.tables, t.lengths) if fused else (t.tables, t.lengths, t.positions, t.physical,
                                                 t.offsets)
-    h_meta = [pin(x) for x in meta]
-    h_out = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in t.q]
-    d_q = [torch.empty_like(x) for x in t.q]
-    d_k = [torch.empty_like(x) for x in t.k]
-    d_v = [torch.empty_like(x) for x in t.v]
-    d_meta = [torch.empty_like(x) for x in meta]
+
+    def packed(tensors, pin):
+        """One buffer holding `tensors` back to back (each part 16-byte
+        aligned), and a view of it shaped like each tensor."""
+        sizes = [x.numel() * x.element_size() for x in tensors]
+        offs, total = [], 0
+        for n in sizes:
+            offs.append(total)
+            total += (n + 15) // 16 * 16
+        buf = (torch.empty(total, dtype=torch.uint8, pin_memory=True) if pin
+               else torch.empty(total, dtype=torch.uint8, device=device))
+        views = [buf[o:o + n].view(x.dtype).view(x.shape) for x, o, n in zip(tensors, offs, sizes)]
+        return buf, views
+
+    inner = 4
+    sizes = [1] + [inner] * ((L - 2) // inner) + ([(L - 2) % inner] if (L - 2) % inner else [])
+    sizes = (sizes + [1]) if L > 1 else [1]
+    groups, first = [], 0
+    for n in sizes:
+        groups.append(list(range(first, first + n)))
+        first += n
+    assert first == L
+    # inputs: per group [q, k, v of each layer]; outputs: per group [out of each layer]
+    h_in, d_in, h_outb, d_outb = [], [], [], []
+    d_q, d_k, d_v, d_out, h_out = [None] * L, [None] * L, [None] * L, [None] * L, [None] * L
+    for grp in groups:
+        parts = [x for layer in grp for x in (t.q[layer], t.k[layer], t.v[layer])]
+        hb, hv = packed(parts, True)
+        db, dv = packed(parts, False)
+        for i, layer in enumerate(grp):
+            for j in range(3):
+                hv[3 * i + j].copy_(parts[3 * i + j])
+            d_q[layer], d_k[layer], d_v[layer] = dv[3 * i], dv[3 * i + 1], dv[3 * i + 2]
+        h_in.append(hb)
+        d_in.append(db)
+        outs = [t.q[layer] for layer in grp]
+        ob, ov = packed(outs, True)
+        dob, dov = packed(outs, False)
+        for i, layer in enumerate(grp):
+            h_out[layer], d_out[layer] = ov[i], dov[i]
+        h_outb.append(ob)
+        d_outb.append(dob)
+    h_meta_b, h_meta = packed(list(meta), True)
+    for hm, x in zip(h_meta, meta):
+        hm.copy_(x)
+    d_meta_b, d_meta = packed(list(meta), False)
     q_out = [torch.empty_like(x) for x in t.q]
     k_out = [torch.empty_like(x) for x in t.k]
-    d_out = [torch.empty_like(x) for x in t.q]
     comp = torch.cuda.Stream(device)
     h2d = torch.cuda.Stream(device)
     d2h = torch.cuda.Stream(device)
-    # Copies move in groups of GE layers: the kernels of one group run back to
-    # back (no copy dependency between them, so consecutive launches overlap
-    # through programmatic dependent launch) while the next group's inputs
-    # are copied in and the previous group's outputs copied out.
-    GE = 4
-    groups = [list(range(g, min(g + GE, L))) for g in range(0, L, GE)]
     copied = [torch.cuda.Event() for _ in range(len(groups) + 1)]
     done = [torch.cuda.Event() for _ in range(len(groups))]
-    h2d_bytes = sum(x.numel() * x.element_size() for x in h_q + h_k + h_v + h_meta)
-    d2h_bytes = sum(x.numel() * x.element_size() for x in h_out)
+    h2d_bytes = sum(x.numel() * x.element_size() for x in list(t.q) + list(t.k) + list(t.v)
+                    + list(meta))
+    d2h_bytes = sum(x.numel() * x.element_size() for x in t.q)
 
     def step():
         with torch.cuda.stream(h2d):
             h2d.wait_stream(comp)  # previous step's kernels no longer read the buffers
-            for dm, hm in zip(d_meta, h_meta):
-                dm.copy_(hm, non_blocking=True)
+            d_meta_b.copy_(h_meta_b, non_blocking=True)
             copied[-1].record(h2d)
-            for gi, grp in enumerate(groups):
-                for layer in grp:
-                    d_q[layer].copy_(h_q[layer], non_blocking=True)
-                    d_k[layer].copy_(h_k[layer], non_blocking=True)
-                    d_v[layer].copy_(h_v[layer], non_blocking=True)
+            for gi in range(len(groups)):
+                d_in[gi].copy_(h_in[gi], non_blocking=True)
                 copied[gi].record(h2d)
         comp.wait_event(copied[-1])
         tables, lengths = d_meta[0], d_meta[1]
@@ -344,8 +372,7 @@ def e2e_run(w, t, steps, warmup, device):
             done[gi].record(comp)
             with torch.cuda.stream(d2h):
                 d2h.wait_event(done[gi])
-                for layer in grp:
-                    h_out[layer].copy_(d_out[layer], non_blocking=True)
+                h_outb[gi].copy_(d_outb[gi], non_blocking=True)
         comp.wait_stream(d2h)
 
     # The step (copies on their streams + ops) is captured as one CUDA graph,
@@ -502,8 +529,9 @@ def run_ours(args):
         ms_e2e = max_over_ranks(ms_e2e, world, device)
         e2e = {"value": full.batch / (ms_e2e * 1e-3), "unit": UNIT, "ms_per_step": ms_e2e,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "public ops with pinned host buffers, H2D/D2H on copy streams in "
-                       "groups of 4 layers, "
+               "path": "public ops with pinned host buffers; one H2D and one D2H copy per "
+                       "layer group on copy streams (groups of 4 layers, single-layer first "
+                       "and last groups), "
                        f"step launched as {'one CUDA graph' if e2e_mode == 'graph' else 'eager calls'}"}
 
     # the other even split, measured the same way (N > 1 only)
