@@ -598,9 +598,11 @@ prefill_tc_kernel(const PrefillTcParams p, const __grid_constant__ CUtensorMap q
         const int k0 = j * BN;
         if (k0 + BN > it.t0 || k0 + BN > kend) {  // diagonal or last tile: mask
           const int lim = qr + 1 < kend ? qr + 1 : kend;  // keys [0, lim) are visible
+          if (k0 + BN > lim) {  // rows that see the whole tile skip the selects
 #pragma unroll
-          for (int i = 0; i < BN; ++i)
-            if (k0 + i >= lim) sc[i] = -INFINITY;
+            for (int i = 0; i < BN; ++i)
+              if (k0 + i >= lim) sc[i] = -INFINITY;
+          }
         }
         static_assert(BN == 64, "the max and exponent loops below are written for 64 keys");
         float mx8[8];  // independent chains of three-input max
