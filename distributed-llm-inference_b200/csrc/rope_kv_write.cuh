@@ -493,14 +493,17 @@ __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
   }
 }
 
-// Prefill after the valid-mask scan, vectorised layouts: ROWS rows per CTA.
-// The rows' q, k and v are staged into shared memory with cp.async at entry,
-// so those loads are in flight while the positions and cos/sin are computed;
-// q and k are then rotated from shared memory and stored to q_out / k_out,
-// the rotated k also back into shared memory. None of this needs the scan,
-// so it runs before the dependency wait; after it, each row's slot is
-// resolved and the rotated k and the v row are copied to it from shared
-// memory.
+// Prefill after the valid-mask scan, vectorised layouts: ROWS rows per CTA,
+// each row owned by its own group of 8 / ROWS warps from start to end (one
+// warp per row at 8 rows per CTA), so the phases of one row never wait for
+// another row: the groups synchronise on their own named barrier (a warp
+// barrier for single-warp groups), never on the whole CTA. A group stages its
+// row's q, k and v into shared memory with cp.async at entry, so those loads
+// are in flight while the row's position and cos/sin are computed; q and k
+// are then rotated from shared memory and stored to q_out / k_out, the
+// rotated k also back into shared memory. None of this needs the scan, so it
+// runs before the dependency wait; after it, the row's slot is resolved and
+// the rotated k and the v row are copied to it from shared memory.
 // HQ, HK, DIM: the head counts and head_dim as compile-time constants for
 // the common shapes (0: taken from p), which turns the index arithmetic's
 // divisions into multiplications.
@@ -508,73 +511,76 @@ template <typename T, int ROWS, int HQ = 0, int HK = 0, int DIM = 0>
 __global__ void __launch_bounds__(256) rope_prefill_vec_kernel(RopeParams p) {
   launch_dependents();
   constexpr int VEC = 16 / (int)sizeof(T);
-  extern __shared__ float cs[];  // [ROWS][2][dim/2], then the staged rows
+  static_assert(ROWS >= 1 && 8 % ROWS == 0, "whole warp groups of the 256-thread CTA");
+  constexpr int GT = 256 / ROWS;  // threads of a row's group
+  extern __shared__ float cs[];   // [ROWS][2][dim/2], then the staged rows
   __shared__ long long slot_base[ROWS];
   __shared__ float row_fpos[ROWS];
-  const int tid = threadIdx.x;
+  const int g = threadIdx.x / GT, gt = threadIdx.x % GT;
+  auto group_sync = [&] {
+    if constexpr (GT == 32) {
+      __syncwarp();
+    } else {
+      asm volatile("bar.sync %0, %1;\n" ::"r"(1 + g), "r"(GT) : "memory");
+    }
+  };
   const int heads = HQ ? HQ : p.heads, kv_heads = HK ? HK : p.kv_heads;
   const int dim = DIM ? DIM : p.dim;
   const int half = dim >> 1, hchunks = half / VEC;
   const int qc = heads * dim / VEC, kc = kv_heads * dim / VEC;  // chunks per q / k row
   const int row_chunks = qc + 2 * kc;                                    // q, k, v
-  uint4* stg = reinterpret_cast<uint4*>(cs + ROWS * dim);               // [ROWS][row_chunks]
-  const int64_t r0 = (int64_t)blockIdx.x * ROWS;
-  const int nrows = p.num_rows - r0 < ROWS ? (int)(p.num_rows - r0) : ROWS;
-  for (int i = tid; i < nrows * row_chunks; i += blockDim.x) {
-    const int rr = i / row_chunks, c = i - rr * row_chunks;
-    const int64_t r = r0 + rr;
+  uint4* stg = reinterpret_cast<uint4*>(cs + ROWS * dim) + (size_t)g * row_chunks;  // this row
+  float* rcs = cs + g * dim;  // this row's cos [half], sin [half]
+  const int64_t r = (int64_t)blockIdx.x * ROWS + g;
+  if (r >= p.num_rows) return;  // the whole group: no barrier of it follows
+  for (int c = gt; c < row_chunks; c += GT) {
     const uint4* src = c < qc ? static_cast<const uint4*>(p.q) + r * qc + c
                        : c < qc + kc ? static_cast<const uint4*>(p.k) + r * kc + (c - qc)
                                      : static_cast<const uint4*>(p.v) + r * kc + (c - qc - kc);
-    cp_async16(stg + i, src, true);
+    cp_async16(stg + c, src, true);
   }
   cp_async_commit();
-  if (tid < nrows) {
-    const int64_t r = r0 + tid;
+  if (gt == 0) {
     const int64_t bi = r / p.seq, si = r - bi * p.seq;
-    row_fpos[tid] = (float)p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
+    row_fpos[g] = (float)p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
   }
-  __syncthreads();
-  for (int i = tid; i < nrows * half; i += blockDim.x) {
-    const int rr = i / half, j = i - rr * half;
+  group_sync();
+  for (int j = gt; j < half; j += GT) {
     float c, s;
-    rope_cos_sin<T>(__fmul_rn(row_fpos[rr], p.inv_freq[j]), &c, &s);
-    cs[(rr * 2) * half + j] = Elem<T>::to_f(Elem<T>::from_f(c));
-    cs[(rr * 2 + 1) * half + j] = Elem<T>::to_f(Elem<T>::from_f(s));
+    rope_cos_sin<T>(__fmul_rn(row_fpos[g], p.inv_freq[j]), &c, &s);
+    rcs[j] = Elem<T>::to_f(Elem<T>::from_f(c));
+    rcs[half + j] = Elem<T>::to_f(Elem<T>::from_f(s));
   }
   cp_async_wait<0>();
-  __syncthreads();
+  group_sync();
   const int qpairs = heads * hchunks, rot_row = qpairs + kv_heads * hchunks;
-  for (int i = tid; i < nrows * rot_row; i += blockDim.x) {
-    const int rr = i / rot_row, w = i - rr * rot_row;
-    const int64_t r = r0 + rr;
+  for (int w = gt; w < rot_row; w += GT) {
     const bool isq = w < qpairs;
     const int ww = isq ? w : w - qpairs;
     const int h = ww / hchunks, c = ww - h * hchunks;
-    T* in = reinterpret_cast<T*>(stg + (size_t)rr * row_chunks + (isq ? 0 : qc)) + h * dim;
+    T* in = reinterpret_cast<T*>(stg + (isq ? 0 : qc)) + h * dim;
     T* out = isq ? static_cast<T*>(p.q_out) + (r * heads + h) * dim
                  : static_cast<T*>(p.k_out) + (r * kv_heads + h) * dim;
     uint4 o1, o2;
-    rope_chunk_pair<T>(in, c * VEC, half, cs + (rr * 2) * half, cs + (rr * 2 + 1) * half, o1, o2);
+    rope_chunk_pair<T>(in, c * VEC, half, rcs, rcs + half, o1, o2);
     store_chunk_pair<T>(out, c * VEC, half, o1, o2);
     if (!isq) store_chunk_pair<T>(in, c * VEC, half, o1, o2);  // this thread's chunks only
   }
   grid_dependency_wait();  // slot_of_row comes from the scan
-  if (tid < nrows) {
+  if (gt == 0) {
     long long base = -1;
     int64_t pos = 0;
     int len = 0;
-    resolve_row(p, r0 + tid, &pos, &base, &len);
-    slot_base[tid] = base;
+    resolve_row(p, r, &pos, &base, &len);
+    slot_base[g] = base;
   }
-  __syncthreads();  // slots and the rotated k rows in shared memory
-  const int cp_row = 2 * kc;  // rotated k, then v
-  for (int i = tid; i < nrows * cp_row; i += blockDim.x) {
-    const int rr = i / cp_row, c = i - rr * cp_row;
-    if (slot_base[rr] < 0) continue;
+  group_sync();  // the slot and the rotated k row in shared memory
+  const long long base = slot_base[g];
+  if (base < 0) return;
+  for (int c = gt; c < 2 * kc; c += GT) {  // rotated k, then v
     const bool isk = c < kc;
-    T* dst = static_cast<T*>(isk ? p.k_pool : p.v_pool) + slot_base[rr];
-    reinterpret_cast<uint4*>(dst)[isk ? c : c - kc] = stg[(size_t)rr * row_chunks + qc + c];
+    T* dst = static_cast<T*>(isk ? p.k_pool : p.v_pool) + base;
+    reinterpret_cast<uint4*>(dst)[isk ? c : c - kc] = stg[qc + c];
   }
 }
 
