@@ -620,8 +620,10 @@ def run_ours(args):
 # blocks per warp), or the FP32 SIMT kernel.
 def attn_kernel_label(head_dim: int, fused: bool, dtype: torch.dtype = torch.float16) -> str:
     if dtype == torch.float32:
-        return (f"attn_tma_dyn_kernel<SimtMath<float,{head_dim},4,2,TMA>>: FP32 SIMT inner "
-                "loop (fp32 FMA throughout), TMA producer warp, stream-K with a dynamic tail, "
+        return (f"attn_tma_dyn_kernel<SimtMath<float,{head_dim},4,2,TMA>"
+                f"{', fused prologue' if fused else ''}>: "
+                f"{'RoPE + KV-slot write + attention, ' if fused else ''}FP32 SIMT inner loop "
+                "(fp32 FMA throughout), TMA producer warp, stream-K with a dynamic tail, "
                 "epilogue warp")
     m = "MmaMath<128,4,3,TMA>" if head_dim == 128 else f"MmaMath<{head_dim},4,3,TMA,2>"
     if fused:

@@ -380,6 +380,7 @@ struct MmaMath {
   static constexpr int D = D_, GP = GQ_, STAGES = STAGES_, LAYOUT = LAYOUT_, SUB = SUB_;
   static_assert(SUB_ == 1 || LAYOUT_ == kTma128B, "multi-block tiles are staged by TMA");
   static constexpr int NW = 4, NT = 128;
+  static constexpr bool kSimt = false;   // tensor-core inner loop
   static constexpr int WT = 16 * SUB;    // tokens per warp per tile (SUB x MMA M)
   static constexpr int CHUNKS = D / 8;   // 16-byte chunks of a K/V row
   static constexpr int TILE = NW * WT;   // 64 * SUB tokens
@@ -584,6 +585,7 @@ struct SimtMath {
   static constexpr int DL = CPL * VEC;         // dims per lane (QK)
   static constexpr int TPW = 32 / LPT;         // lane groups per warp
   static constexpr int NW = 4, NT = 128;
+  static constexpr bool kSimt = true;       // fp32 FMA inner loop
   static constexpr int TW = TPW * TPG;      // tokens per warp per tile
   static constexpr int WT = TW;
   static constexpr int TILE = NW * TW;      // tokens per tile

@@ -371,6 +371,54 @@ __device__ __forceinline__ void fused_piece_start(typename M::State& st, const A
   }
 }
 
+// The fused prologue's piece start for the SIMT inner loop (FP32): the
+// cos/sin table of the piece's position (rebuilt only when the position
+// changes), then the group's G query rows rotated into `rq` (shared memory;
+// it may be the rows' own prefetch slot, each chunk pair is read and written
+// by one thread) and, for the piece holding the new token, the token's
+// rotated k and its v into `newrow`; then the SIMT state is loaded from `rq`.
+// The rotation is rope_chunk_pair, the cos/sin rope_cos_sin of the position
+// times inv_freq: the operations of the decode prologue kernel, so the fused
+// layer equals rope_kv_write_decode + paged_attention bit for bit. q, k and v
+// rows are read in 16-byte chunks (16-byte aligned rows).
+template <class M, class Sync>
+__device__ __forceinline__ void fused_piece_start_simt(
+    typename M::State& st, const AttnParams& p, const typename M::T* qbase,
+    const typename M::T* knew, const typename M::T* vnew, int pos, bool new_tok,
+    const float* invf, float* cs, typename M::T* newrow, typename M::T* rq, int& cs_pos,
+    Sync sync) {
+  using T = typename M::T;
+  constexpr int D = M::D, HALF = D / 2, VEC = 16 / (int)sizeof(T), HC = HALF / VEC;
+  constexpr int NMT = M::NW * 32;  // math threads
+  const int tid = threadIdx.x;
+  if (pos != cs_pos) {
+    for (int j = tid; j < HALF; j += NMT) {
+      float c, s;
+      rope_cos_sin<T>(__fmul_rn((float)pos, invf[j]), &c, &s);
+      cs[j] = Elem<T>::to_f(Elem<T>::from_f(c));
+      cs[HALF + j] = Elem<T>::to_f(Elem<T>::from_f(s));
+    }
+    cs_pos = pos;
+    sync();
+  }
+  const int nq = p.G * HC, nk = new_tok ? HC : 0;
+  for (int i = tid; i < nq + nk; i += NMT) {
+    const bool isq = i < nq;
+    const int ii = isq ? i : i - nq;
+    const int g = ii / HC, c = ii - g * HC;
+    uint4 o1, o2;
+    rope_chunk_pair<T>(isq ? qbase + g * D : knew, c * VEC, HALF, cs, cs + HALF, o1, o2);
+    store_chunk_pair<T>(isq ? rq + g * D : newrow, c * VEC, HALF, o1, o2);
+  }
+  if (new_tok) {
+    for (int i = tid; i < D / VEC; i += NMT)
+      reinterpret_cast<uint4*>(newrow + D)[i] = reinterpret_cast<const uint4*>(vnew)[i];
+  }
+  fence_proxy_async_smem();  // rq may be a prefetch slot the next bulk copy refills
+  sync();
+  M::begin_piece_at(st, rq, p.G);
+}
+
 template <class M>
 struct DynStreamK {
   static_assert(M::LAYOUT == kTma128B, "dynamic kernel stages with TMA");
@@ -394,7 +442,7 @@ struct DynStreamK {
     return 1024 + (size_t)STAGES * (M::STAGE_BYTES + QPRE_BYTES + KVPRE_BYTES) + EXTRA_BYTES +
            (size_t)(4 * B + 1 + kDynMisc) * 4 + (2 * STAGES + 2 * kHandoffDepth) * 8 + 16 +
            (size_t)STAGES * sizeof(TileRecord) + kHandoffDepth * sizeof(PieceHandoff) +
-           (size_t)D * 4 + (size_t)2 * D * 2 + (size_t)D / 2 * 4 +
+           (size_t)D * 4 + (size_t)2 * D * E + (size_t)D / 2 * 4 +
            64;  // + fused prologue: cos/sin, new row, inv_freq (+ alignment)
   }
   // partial slots: two per worker (static workers + tail chunks)
@@ -412,6 +460,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
   constexpr int D = M::D, GP = M::GP, NW = M::NW, STAGES = M::STAGES, NT = K::NT;
   constexpr int TILE = M::TILE, TU = M::TILE_UNITS;
   constexpr int SLOT_FLOATS = GP * (D + 2);
+  static_assert(!FUSE || M::CHUNKS <= 32, "one 16-byte chunk of the new token's row per lane");
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -438,7 +487,7 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
     return (reinterpret_cast<uintptr_t>(q) + 15) & ~uintptr_t(15);
   };
   float* cs_tab = reinterpret_cast<float*>(align16(hand + kHandoffDepth));  // [2][D/2]
-  __half* newrow = reinterpret_cast<__half*>(align16(cs_tab + D));          // k[D], v[D]
+  T* newrow = reinterpret_cast<T*>(align16(cs_tab + D));                    // k[D], v[D]
   float* invf = reinterpret_cast<float*>(align16(newrow + 2 * D));          // [D/2]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -609,8 +658,9 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
           if (kvp) {
             const int64_t kvo = (int64_t)bq * p.kv_row + (int64_t)c.h * D;
             unsigned char* dst = kvpre + (size_t)s * K::KVPRE_BYTES;
-            bulk_load(dst, static_cast<const __half*>(p.k_new) + kvo, D * 2, &full[s]);
-            bulk_load(dst + D * 2, static_cast<const __half*>(p.v_new) + kvo, D * 2, &full[s]);
+            bulk_load(dst, static_cast<const T*>(p.k_new) + kvo, D * K::E, &full[s]);
+            bulk_load(dst + D * K::E, static_cast<const T*>(p.v_new) + kvo, D * K::E,
+                      &full[s]);
           }
         }
         __syncwarp();
@@ -711,12 +761,19 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
             : static_cast<const T*>(p.q) + (int64_t)r.b * p.q_row + (int64_t)r.h * p.G * D;
     if constexpr (FUSE) {
       if (r.flags & kRecFirst) {
-        const __half* kvs = reinterpret_cast<const __half*>(kvpre + (size_t)s * K::KVPRE_BYTES);
+        const T* kvs = reinterpret_cast<const T*>(kvpre + (size_t)s * K::KVPRE_BYTES);
         const int64_t kvo = (int64_t)r.b * p.kv_row + (int64_t)r.h * D;
-        fused_piece_start<M>(st, p, qbase, pre ? kvs : static_cast<const __half*>(p.k_new) + kvo,
-                             pre ? kvs + D : static_cast<const __half*>(p.v_new) + kvo,
-                             r.len - 1, (r.flags & kRecNewTok) != 0, invf, cs_tab, newrow,
-                             cs_pos, sync_math);
+        const T* kn = pre ? kvs : static_cast<const T*>(p.k_new) + kvo;
+        const T* vn = pre ? kvs + D : static_cast<const T*>(p.v_new) + kvo;
+        if constexpr (M::kSimt) {
+          fused_piece_start_simt<M>(st, p, qbase, kn, vn, r.len - 1,
+                                    (r.flags & kRecNewTok) != 0, invf, cs_tab, newrow,
+                                    reinterpret_cast<T*>(qpre + (size_t)s * K::QPRE_BYTES),
+                                    cs_pos, sync_math);
+        } else {
+          fused_piece_start<M>(st, p, qbase, kn, vn, r.len - 1, (r.flags & kRecNewTok) != 0,
+                               invf, cs_tab, newrow, cs_pos, sync_math);
+        }
       }
       // The new token's row of this tile: the TMA brought the slot's old
       // bytes; the owning warp writes the rotated k and the v in their place
@@ -724,16 +781,16 @@ attn_tma_dyn_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap
       // slot from global memory).
       const int nr = r.ntok - 1;
       if ((r.flags & kRecNewRow) && nr >= r0 && nr < r0 + M::WT) {
-        if (lane < D / 8) {
+        if (lane < M::CHUNKS) {
           const uint4 kc = reinterpret_cast<const uint4*>(newrow)[lane];
           const uint4 vc = reinterpret_cast<const uint4*>(newrow + D)[lane];
           *reinterpret_cast<uint4*>(sk + M::offset(nr, lane)) = kc;
           *reinterpret_cast<uint4*>(sv + M::offset(nr, lane)) = vc;
           if (r.slot_row >= 0) {
             const int64_t base = ((int64_t)r.slot_row * KVH + r.h) * D;
-            reinterpret_cast<uint4*>(static_cast<__half*>(const_cast<void*>(p.k_pool)) +
+            reinterpret_cast<uint4*>(static_cast<T*>(const_cast<void*>(p.k_pool)) +
                                      base)[lane] = kc;
-            reinterpret_cast<uint4*>(static_cast<__half*>(const_cast<void*>(p.v_pool)) +
+            reinterpret_cast<uint4*>(static_cast<T*>(const_cast<void*>(p.v_pool)) +
                                      base)[lane] = vc;
           }
         }

@@ -288,6 +288,30 @@ bool pick_dyn_f32_gp(int G, FastKernel* out) {
   }
   return false;
 }
+// The same FP32 kernels with the decode prologue folded in (decode_attention).
+template <int D, int GP>
+FastKernel dyn_simt_f32_fused() {
+  if constexpr (D == 128) return make_dyn_fused<pdb::SimtMath<float, D, GP, 2, 3, pdb::kTma128B>>();
+  else return make_dyn_fused<pdb::SimtMath<float, D, GP, 4, 3, pdb::kTma128B>>();
+}
+template <int D>
+bool pick_dyn_f32_fused_gp(int G, FastKernel* out) {
+  if (G <= 1) { *out = dyn_simt_f32_fused<D, 1>(); return true; }
+  if (G <= 2) { *out = dyn_simt_f32_fused<D, 2>(); return true; }
+  if (G <= 4) { *out = dyn_simt_f32_fused<D, 4>(); return true; }
+  if constexpr (D <= 64) {
+    if (G <= 8) { *out = dyn_simt_f32_fused<D, 8>(); return true; }
+  }
+  return false;
+}
+bool pick_dyn_f32_fused(int D, int G, FastKernel* out) {
+  switch (D) {
+    case 64: return pick_dyn_f32_fused_gp<64>(G, out);
+    case 128: return pick_dyn_f32_fused_gp<128>(G, out);
+    default: return false;
+  }
+}
+
 bool pick_dyn_f32(int D, int G, FastKernel* out) {
   switch (D) {
     case 64: return pick_dyn_f32_gp<64>(G, out);
@@ -859,12 +883,16 @@ int pdb_decode_attention_supported(int64_t batch, int64_t heads, int64_t kv_head
                                    int64_t head_dim, int64_t num_blocks, int64_t block_size,
                                    int dtype) {
   FastKernel fk;
-  if (dtype != PDB_DTYPE_FLOAT16 || batch <= 0 || kv_heads <= 0 || heads % kv_heads) return 0;
+  if ((dtype != PDB_DTYPE_FLOAT16 && dtype != PDB_DTYPE_FLOAT32) || batch <= 0 ||
+      kv_heads <= 0 || heads % kv_heads)
+    return 0;
   const bool tma_ok = block_size % pdb::kUnitTokens == 0 &&
                       num_blocks * block_size < (int64_t(1) << 31) &&
                       tensor_map_encoder() != nullptr;
+  const int G = (int)(heads / kv_heads);
   return streamk_shape_ok(batch, kv_heads) && tma_ok &&
-         pick_dyn_fused((int)head_dim, (int)(heads / kv_heads), &fk);
+         (dtype == PDB_DTYPE_FLOAT16 ? pick_dyn_fused((int)head_dim, G, &fk)
+                                     : pick_dyn_f32_fused((int)head_dim, G, &fk));
 }
 
 int pdb_decode_attention(const void* q, const void* k_new, const void* v_new, void* k_pool,
@@ -902,12 +930,22 @@ int pdb_decode_attention_ex(const void* q, const void* k_new, const void* v_new,
   const int64_t kv_row = kv_row_stride ? kv_row_stride : KVH * D;
   if (q_row < H * D || kv_row < KVH * D || (q_row & 1))
     return fail(PDB_ERR_INVALID_ARGUMENT, "invalid row strides");
+  const int esize = dtype == PDB_DTYPE_FLOAT16 ? 2 : 4;
+  const int per16 = 16 / esize;  // elements per 16-byte chunk
+  // FP32 rotates q, k and v in 16-byte chunks: rows 16-byte aligned
+  if (dtype == PDB_DTYPE_FLOAT32 && !(aligned16(q) && aligned16(k_new) && aligned16(v_new) &&
+                                      q_row % per16 == 0 && kv_row % per16 == 0))
+    return fail(PDB_ERR_INVALID_ARGUMENT,
+                "fused FP32 decode attention needs 16-byte aligned q, k and v rows");
   if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return fail(PDB_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   int dev = 0;
   if ((rc = current_device(&dev))) return rc;
   FastKernel fk;
-  pick_dyn_fused((int)D, (int)(H / KVH), &fk);
+  if (dtype == PDB_DTYPE_FLOAT16)
+    pick_dyn_fused((int)D, (int)(H / KVH), &fk);
+  else
+    pick_dyn_f32_fused((int)D, (int)(H / KVH), &fk);
   const int64_t grid = fast_grid(dev, fk, B, KVH, max_length);
   if (grid <= 0) return fail(PDB_ERR_CUDA, "fast kernel cannot be resident on this device");
   const FastWs ws = fast_ws_layout(B, KVH, D, fk, grid);
@@ -934,11 +972,11 @@ int pdb_decode_attention_ex(const void* q, const void* k_new, const void* v_new,
                   ((flags & PDB_DECODE_STABLE_POOLS) ? 2 : 0);
   p.q_row = q_row;
   p.kv_row = kv_row;
-  p.bulk_q = aligned16(q) && q_row % 8 == 0 && aligned16(k_new) && aligned16(v_new) &&
-             kv_row % 8 == 0;
+  p.bulk_q = aligned16(q) && q_row % per16 == 0 && aligned16(k_new) && aligned16(v_new) &&
+             kv_row % per16 == 0;
   CUtensorMap kmap, vmap;
-  if (!(encode_pool_map(&kmap, k_pool, N, bs, KVH, D) &&
-        encode_pool_map(&vmap, v_pool, N, bs, KVH, D)))
+  if (!(encode_pool_map(&kmap, k_pool, N, bs, KVH, D, esize) &&
+        encode_pool_map(&vmap, v_pool, N, bs, KVH, D, esize)))
     return fail(PDB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV pools");
   fk.launch(p, (int)grid, fk.smem((int)B), static_cast<cudaStream_t>(stream), &kmap, &vmap);
   const cudaError_t e = cudaGetLastError();

@@ -275,9 +275,10 @@ def rope_kv_write_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 
 def decode_attention_supported(q: torch.Tensor, k_pool: torch.Tensor) -> bool:
-    """Whether ``decode_attention`` covers this shape (FP16, head_dim 64/128,
-    group <= 8, block_size a multiple of 16) on the current device."""
-    if q.dim() != 3 or k_pool.dim() != 4 or q.dtype != torch.float16:
+    """Whether ``decode_attention`` covers this shape (FP16 or FP32, head_dim
+    64/128, group <= 8 (FP32 head_dim 128: <= 4), block_size a multiple of
+    16) on the current device."""
+    if q.dim() != 3 or k_pool.dim() != 4 or q.dtype not in (torch.float16, torch.float32):
         return False
     B, H, D = q.shape  # q may be a meta tensor: only its shape and dtype are read
     N, bs, KVH, _ = k_pool.shape
@@ -300,8 +301,8 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: 
     slice of one fused q/k/v projection output), lengths already
     counting the new token (its position is lengths[b] - 1). The rotated k
     and v are written to the token's slot; returns the attention output
-    [B, H, D], bit-identical to the two-launch path. FP16 only (see
-    ``decode_attention_supported``).
+    [B, H, D], bit-identical to the two-launch path. FP16 and FP32 (see
+    ``decode_attention_supported``; FP32 rows must be 16-byte aligned).
 
     ``metadata_stable=True`` promises that tables, lengths and inv_freq were
     not written by the previous kernel on the stream (every layer after the

@@ -251,14 +251,15 @@ PDB_API int64_t pdb_debug_partition(const int32_t* lengths, int64_t batch,
 /*
  * One decode layer in one launch: the RoPE + KV-slot write of
  * pdb_rope_kv_write_decode (advance = 0) and the attention of
- * pdb_paged_attention, fused into the FP16 stream-K kernel.
+ * pdb_paged_attention, fused into the stream-K kernel (FP16: tensor-core inner
+ * loop; FP32: fp32 SIMT inner loop, q / k_new / v_new rows 16-byte aligned).
  * Replaces: worker/llama.py:168-174 (rope, the two slot writes, attention)
  * for a decode step, given lengths that already count the new token.
- *   q            FP16 [B, H, D], NOT rotated (the kernel rotates it at
+ *   q            FP16 or FP32 [B, H, D], NOT rotated (the kernel rotates it at
  *                position lengths[b] - 1; q itself is not modified); sequence
  *                b's heads start at q + b * q_row_stride (elements; 0 = H * D,
  *                packed), e.g. a slice of a fused q/k/v projection's output
- *   k_new, v_new FP16 [B, KVH, D], the new token's k (not rotated) and v,
+ *   k_new, v_new [B, KVH, D] of q's dtype, the new token's k (not rotated) and v,
  *                rows kv_row_stride elements apart (0 = KVH * D)
  *   k_pool, v_pool, tables, lengths, max_length, out, workspace: as for
  *                pdb_paged_attention; the new token's rotated k and its v

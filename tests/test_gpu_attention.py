@@ -251,22 +251,27 @@ def test_no_device_errors_raised(pkg, cuda):
     assert pkg.read_device_errors() == 0
 
 
-@pytest.mark.parametrize("shape", ["llama3", "smollm"])
+@pytest.mark.parametrize("shape", ["llama3", "smollm", "smollm_fp32", "llama3_fp32"])
 def test_fused_decode_layer_equals_two_launches(pkg, cuda, shape):
     """decode_attention (RoPE + slot writes folded into the attention kernel)
     is bit-identical to rope_kv_write_decode + paged_attention: same output,
-    same pool bytes everywhere."""
+    same pool bytes everywhere; FP16 (tensor-core inner loop) and FP32 (SIMT
+    inner loop), head_dim 64 and 128."""
+    import dataclasses
     g = torch.Generator().manual_seed(17)
     if shape == "llama3":
         w = W.llama3_8b(batch=96, layers=1)
-        B, H, KVH, D = 96, 32, 8, 128
-    else:
+    elif shape == "llama3_fp32":
+        w = dataclasses.replace(W.llama3_8b(batch=32, layers=1), dtype=torch.float32)
+    elif shape == "smollm":
         w = W.smollm_fp16(batch=64, layers=1)
-        B, H, KVH, D = 64, 9, 3, 64
+    else:
+        w = W.smollm_fp32(batch=64, layers=1)
+    B, H, KVH, D = w.batch, w.heads, w.kv_heads, w.head_dim
     t = W.materialize(w, cuda)
-    q = torch.randn(B, H, D, generator=g).half().to(cuda)
-    k = torch.randn(B, KVH, D, generator=g).half().to(cuda)
-    v = torch.randn(B, KVH, D, generator=g).half().to(cuda)
+    q = torch.randn(B, H, D, generator=g).to(w.dtype).to(cuda)
+    k = torch.randn(B, KVH, D, generator=g).to(w.dtype).to(cuda)
+    v = torch.randn(B, KVH, D, generator=g).to(w.dtype).to(cuda)
     assert pkg.decode_attention_supported(q, t.k_pools[0])
     kp1, vp1 = t.k_pools[0].clone(), t.v_pools[0].clone()
     kp2, vp2 = t.k_pools[0].clone(), t.v_pools[0].clone()
