@@ -366,3 +366,55 @@ def test_fused_decode_stable_metadata_is_identical(pkg, cuda, shape):
         for (kp, vp), (kr, vr) in zip(zip(t.k_pools, t.v_pools), ref_pools):
             assert torch.equal(kp, kr) and torch.equal(vp, vr)
     assert pkg.read_device_errors() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+@pytest.mark.parametrize("H,KVH,D", [(9, 3, 64), (32, 8, 128)])
+def test_fused_decode_boundary_lengths(pkg, cuda, dtype, H, KVH, D):
+    """The fused decode layer at lengths on 16-token unit, page and 64-token
+    tile boundaries (the new token is the first or the last row of its unit,
+    page or tile), up to 8192, over fragmented tables: bit-identical to
+    rope_kv_write_decode + paged_attention (outputs and every pool byte) and
+    within the oracle's tolerance (FP32 1e-5 relative, FP16 2e-3)."""
+    from oracle import rope as orope
+    g = torch.Generator().manual_seed(29 + D)
+    lengths_l = [1, 2, 15, 16, 17, 31, 32, 33, 63, 64, 65, 127, 128, 129, 255, 256, 257,
+                 1000, 4096, 8192]
+    B, bs, max_len = len(lengths_l), 16, 8192
+    lengths = torch.tensor(lengths_l, dtype=torch.int32)
+    pages = [(n + bs - 1) // bs for n in lengths_l]
+    N = sum(pages) + 11
+    perm = torch.randperm(N, generator=g)
+    tables = torch.zeros(B, max(pages), dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(pages):
+        tables[b, :n] = perm[off:off + n].to(torch.int32)
+        off += n
+    kp = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
+    vp = torch.randn(N, bs, KVH, D, generator=g).to(dtype)
+    q = torch.randn(B, H, D, generator=g).to(dtype)
+    kn = torch.randn(B, KVH, D, generator=g).to(dtype)
+    vn = torch.randn(B, KVH, D, generator=g).to(dtype)
+    inv = orope.inv_freq(5e5 if D == 128 else 1e5, D)
+    dq, dkn, dvn = q.to(cuda), kn.to(cuda), vn.to(cuda)
+    dt, dl, dinv = tables.to(cuda), lengths.to(cuda), inv.to(cuda)
+    kp1, vp1 = kp.to(cuda), vp.to(cuda)
+    assert pkg.decode_attention_supported(dq, kp1)
+    kp2, vp2 = kp.to(cuda), vp.to(cuda)
+    fused = pkg.decode_attention(dq, dkn, dvn, kp1, vp1, dt, dl, dinv, max_len)
+    qr_dev, _ = pkg.rope_kv_write_decode(dq, dkn, dvn, kp2, vp2, dt, dl, dinv)
+    two = pkg.paged_attention(qr_dev, kp2, vp2, dt, dl, max_len)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, two)
+    assert torch.equal(kp1, kp2) and torch.equal(vp1, vp2)
+    # against the oracle: rotate on the CPU, write the slots, attend
+    pos = (lengths.to(torch.int64) - 1).unsqueeze(1)
+    phys = tables.to(torch.int64).gather(1, pos // bs)[:, 0]
+    offs = pos[:, 0] % bs
+    qr, kr = orope.rope(q.unsqueeze(1), kn.unsqueeze(1), pos, inv, exact_trig=True)
+    kc, vc = kp.clone(), vp.clone()
+    kc[phys, offs] = kr[:, 0]
+    vc[phys, offs] = vn
+    assert_matches_oracle(fused, qr[:, 0], tables, lengths, (kc, vc), bs,
+                          f"fused decode {dtype} D={D}")
+    assert pkg.read_device_errors() == 0
