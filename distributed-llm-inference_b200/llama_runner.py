@@ -125,7 +125,7 @@ def _tick(runner, cache, token_tensor, tables, lengths, max_length):
     x = runner.model.model.embed_tokens(token_tensor)
     fused = decode_attention_supported(
         torch.empty((batch, runner.heads, runner.head_dim), dtype=runner.dtype,
-                    device="meta"), cache.keys[0]) if runner.dtype == torch.float16 else False
+                    device="meta"), cache.keys[0])
     if fused:
         lengths.add_(1)  # the new token (PagedLlama.decode, worker/llama.py:157-158)
     H, KVH, D = runner.heads, runner.kv_heads, runner.head_dim
