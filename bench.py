@@ -509,16 +509,9 @@ def run_ours(args):
     peak_src = "measured" if peak else "fallback"
     peak = peak or 6650.0
     achieved = attn_bytes / (ms_attn * 1e-3) / 1e9
-    traffic = None
-    # DRAM traffic of the dominant launch: the ncu traffic / algorithmic-bytes
-    # ratio of a smaller capture of the same kernel and workload (the full
-    # launch is too large for a multi-pass capture; traffic grows with the
-    # K/V bytes read), applied to this rank's algorithmic bytes per launch.
-    tf = REPO / "profiles" / "traffic_attn_tma_llama3_b256.json"
-    if tf.exists() and step.fused:
-        tj = json.loads(tf.read_text())
-        if tj.get("workload") == full.name and tj.get("ratio_to_algorithmic"):
-            traffic = int(round(tj["ratio_to_algorithmic"] * attn_bytes))
+    # DRAM traffic of the dominant launch, from a smaller capture of the same
+    # kernel and workload, applied to this rank's algorithmic bytes per launch.
+    traffic = _capture_traffic(full.name, step.fused, attn_bytes)
 
     e2e = None
     if not args.no_e2e:
@@ -678,6 +671,20 @@ def timed_replays(run, stream, device, units: int, min_s: float = 0.3, max_reps:
     return statistics.median(times), clocks.stop(), len(times)
 
 
+def _capture_traffic(workload: str, fused: bool, algorithmic_bytes: float):
+    """DRAM bytes (read + write) of one launch: the ncu traffic /
+    algorithmic-bytes ratio of a committed capture of the same kernel and
+    workload (profiles/traffic_*.json; a full launch is often too large for a
+    multi-pass capture, and traffic grows with the K/V bytes read), applied
+    to these algorithmic bytes. None without such a capture."""
+    for f in sorted((REPO / "profiles").glob("traffic_*.json")):
+        tj = json.loads(f.read_text())
+        if (tj.get("workload") == workload and tj.get("fused", True) == fused
+                and tj.get("ratio_to_algorithmic")):
+            return int(round(tj["ratio_to_algorithmic"] * algorithmic_bytes))
+    return None
+
+
 def measure_decode(w, device, steps: int, warmup: int) -> dict:
     """Decode steps of workload `w` (every layer: RoPE + KV-slot write +
     attention) through the public ops, one CUDA graph per step, K steps per
@@ -720,6 +727,7 @@ def measure_decode(w, device, steps: int, warmup: int) -> dict:
            "roofline": _roofline(nbytes / (ms_launch * 1e-3) / 1e9, "hbm", kernel,
                                  algorithmic_bytes_per_launch=nbytes, ms_per_launch=ms_launch),
            "clocks": clk, "gpu_launches": steps * w.layers * (1 if step.fused else 2)}
+    res["roofline"]["traffic"] = _capture_traffic(w.name, step.fused, nbytes)
     del g_step, g_dom, step, t
     torch.cuda.empty_cache()
     return res
