@@ -152,6 +152,43 @@ struct RopeParams {
 // outside the table raises PDB_DEVERR_LENGTH, a page outside the pool
 // PDB_DEVERR_TABLE_ENTRY; the row's write is then skipped.
 // Without metadata: positions / physical / offsets / slot_of_row as given.
+// Position of row r = (b, s) of the [batch, seq] input. Both entry points
+// reject 2^31 rows or more, so b and s come from a 32-bit division.
+__device__ __forceinline__ int64_t row_position(const RopeParams& p, int64_t r) {
+  const uint32_t rr = (uint32_t)r, sq = (uint32_t)p.seq;
+  const uint32_t bi = rr / sq, si = rr - bi * sq;
+  return p.positions[(int64_t)bi * p.pos_stride_b + (int64_t)si * p.pos_stride_s];
+}
+
+// Slot of row r: its index among the valid rows (slot_of_row, -1 for a
+// padding row), or r itself when every row is written.
+__device__ __forceinline__ int64_t row_slot(const RopeParams& p, int64_t r) {
+  return p.slot_of_row ? (int64_t)p.slot_of_row[r] : r;
+}
+
+// Element offset of the pool row at (physical block, offset), or -1 with
+// PDB_DEVERR_SLOT raised when either lies outside the pool.
+__device__ __forceinline__ long long slot_element_base(const RopeParams& p, int64_t phys,
+                                                       int64_t off) {
+  if (phys < 0 || phys >= p.num_blocks || off < 0 || off >= p.block_size) {
+    raise_error(0x4u);
+    return -1;
+  }
+  return (phys * p.block_size + off) * p.kv_heads * p.dim;
+}
+
+// Element offset of row r's pool slot (-1: no write). A slot beyond
+// num_slots raises PDB_DEVERR_VALID_COUNT.
+__device__ __forceinline__ long long resolve_slot(const RopeParams& p, int64_t r) {
+  const int64_t slot = row_slot(p, r);
+  if (slot < 0) return -1;
+  if (slot >= p.num_slots) {
+    raise_error(0x8u);
+    return -1;
+  }
+  return slot_element_base(p, p.physical[slot], p.offsets[slot]);
+}
+
 __device__ __forceinline__ void resolve_row(const RopeParams& p, int64_t r, int64_t* pos_out,
                                             long long* base_out, int* len_out) {
   long long base = -1;
@@ -173,21 +210,8 @@ __device__ __forceinline__ void resolve_row(const RopeParams& p, int64_t r, int6
       }
     }
   } else {
-    const int64_t bi = r / p.seq, si = r - bi * p.seq;
-    pos = p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
-    const int64_t slot = p.slot_of_row ? (int64_t)p.slot_of_row[r] : r;
-    if (slot >= 0) {
-      if (slot < p.num_slots) {
-        const int64_t phys = p.physical[slot], off = p.offsets[slot];
-        if (phys < 0 || phys >= p.num_blocks || off < 0 || off >= p.block_size) {
-          raise_error(0x4u);
-        } else {
-          base = (phys * p.block_size + off) * p.kv_heads * p.dim;
-        }
-      } else {
-        raise_error(0x8u);
-      }
-    }
+    pos = row_position(p, r);
+    base = resolve_slot(p, r);
   }
   *pos_out = pos;
   *base_out = base;
@@ -388,10 +412,7 @@ __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
     long long base = -1;
     int64_t pos = 0;
     if (p.after_scan) {  // the slot is resolved after the dependency wait
-      if (r < p.num_rows) {
-        const int64_t bi = r / p.seq, si = r - bi * p.seq;
-        pos = p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
-      }
+      if (r < p.num_rows) pos = row_position(p, r);
     } else if (r < p.num_rows) {
       int len = 0;
       resolve_row(p, r, &pos, &base, &len);
@@ -439,13 +460,7 @@ __global__ void __launch_bounds__(256) rope_kv_write_vec_kernel(RopeParams p) {
     __syncthreads();         // every thread's k_out stores precede the slot copies
     if (threadIdx.x < ROWS) {
       const int64_t r = r0 + threadIdx.x;
-      long long base = -1;
-      if (r < p.num_rows) {
-        int64_t pos = 0;
-        int len = 0;
-        resolve_row(p, r, &pos, &base, &len);
-      }
-      slot_base[threadIdx.x] = base;
+      slot_base[threadIdx.x] = r < p.num_rows ? resolve_slot(p, r) : -1;
     }
     __syncthreads();
     // the rotated k row (from k_out) and the v row, each 2*kchunks chunks
@@ -533,17 +548,18 @@ __global__ void __launch_bounds__(256) rope_prefill_vec_kernel(RopeParams p) {
   float* rcs = cs + g * dim;  // this row's cos [half], sin [half]
   const int64_t r = (int64_t)blockIdx.x * ROWS + g;
   if (r >= p.num_rows) return;  // the whole group: no barrier of it follows
-  for (int c = gt; c < row_chunks; c += GT) {
-    const uint4* src = c < qc ? static_cast<const uint4*>(p.q) + r * qc + c
-                       : c < qc + kc ? static_cast<const uint4*>(p.k) + r * kc + (c - qc)
-                                     : static_cast<const uint4*>(p.v) + r * kc + (c - qc - kc);
-    cp_async16(stg + c, src, true);
+  {
+    const uint4* qs = static_cast<const uint4*>(p.q) + r * qc;
+    const uint4* ks = static_cast<const uint4*>(p.k) + r * kc;
+    const uint4* vs = static_cast<const uint4*>(p.v) + r * kc;
+    for (int c = gt; c < qc; c += GT) cp_async16(stg + c, qs + c, true);
+    for (int c = gt; c < kc; c += GT) {
+      cp_async16(stg + qc + c, ks + c, true);
+      cp_async16(stg + qc + kc + c, vs + c, true);
+    }
   }
   cp_async_commit();
-  if (gt == 0) {
-    const int64_t bi = r / p.seq, si = r - bi * p.seq;
-    row_fpos[g] = (float)p.positions[bi * p.pos_stride_b + si * p.pos_stride_s];
-  }
+  if (gt == 0) row_fpos[g] = (float)row_position(p, r);  // positions.float(): round-to-nearest
   group_sync();
   for (int j = gt; j < half; j += GT) {
     float c, s;
@@ -567,13 +583,7 @@ __global__ void __launch_bounds__(256) rope_prefill_vec_kernel(RopeParams p) {
     if (!isq) store_chunk_pair<T>(in, c * VEC, half, o1, o2);  // this thread's chunks only
   }
   grid_dependency_wait();  // slot_of_row comes from the scan
-  if (gt == 0) {
-    long long base = -1;
-    int64_t pos = 0;
-    int len = 0;
-    resolve_row(p, r, &pos, &base, &len);
-    slot_base[g] = base;
-  }
+  if (gt == 0) slot_base[g] = resolve_slot(p, r);
   group_sync();  // the slot and the rotated k row in shared memory
   const long long base = slot_base[g];
   if (base < 0) return;
