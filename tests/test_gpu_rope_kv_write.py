@@ -189,15 +189,19 @@ def test_rope_vector_and_scalar_paths(pkg, cuda, dtype, D):
     assert torch.equal(kd.cpu(), exp_k) and torch.equal(vd.cpu(), exp_v)
 
 
+@pytest.mark.parametrize("shape", [(21, 9, 3, 64), (24, 32, 8, 128)], ids=["smollm", "llama3"])
 @pytest.mark.parametrize("shared_positions", [True, False])
-def test_rope_many_short_rows(pkg, cuda, shared_positions):
-    """Many short rows (here 21 sequences x 120 positions, SmolLM2 heads: more
-    than 2048 rows of 72 16-byte work items) take the 8-rows-per-CTA launch;
-    with positions shared across sequences (a prefill batch) and with
-    sequences at different offsets, outputs match the oracle, the valid rows'
-    slots hold the rotated k and the input v, and nothing else is written."""
+def test_rope_many_short_rows(pkg, cuda, shared_positions, shape):
+    """Many short rows: 21 sequences x 120 positions with SmolLM2 heads (more
+    than 2048 rows of 72 16-byte work items: 8 rows per CTA, one warp per
+    row), and 24 x 120 with Llama-3-8B heads (2 rows per CTA, four warps per
+    row on named barriers, 1,440 CTAs: more than are resident at once). With
+    positions shared across sequences (a prefill batch) and with sequences
+    at different offsets, outputs match the oracle, the valid rows' slots
+    hold the rotated k and the input v, and nothing else is written."""
     g = torch.Generator().manual_seed(31 if shared_positions else 32)
-    B, S, H, KVH, D, N, bs = 21, 120, 9, 3, 64, 200, 16
+    B, H, KVH, D = shape
+    S, N, bs = 120, 200, 16
     q = torch.randn(B, S, H, D, generator=g).half()
     k = torch.randn(B, S, KVH, D, generator=g).half()
     v = torch.randn(B, S, KVH, D, generator=g).half()
