@@ -418,3 +418,46 @@ def test_fused_decode_boundary_lengths(pkg, cuda, dtype, H, KVH, D):
     assert_matches_oracle(fused, qr[:, 0], tables, lengths, (kc, vc), bs,
                           f"fused decode {dtype} D={D}")
     assert pkg.read_device_errors() == 0
+
+
+def test_fused_decode_row_alignment(pkg, cuda):
+    """q, k and v rows given as slices of wider rows. FP32 rotates 16-byte
+    chunks, so its rows must be 16-byte aligned: a q row stride of H*D + 2
+    floats, or a k starting 8 bytes into its buffer, is rejected with the
+    library's message before anything is written. FP16 reads q in 4-byte
+    pairs and takes the same q stride, with the packed call's result and
+    pool bytes."""
+    from oracle import rope as orope
+    B, H, KVH, D, N, bs = 3, 6, 2, 64, 24, 16
+    g = torch.Generator().manual_seed(41)
+    tables = torch.tensor([[9, 2, 5], [1, 8, 4], [7, 0, 6]], dtype=torch.int32).to(cuda)
+    lengths = torch.tensor([1, 17, 35], dtype=torch.int32).to(cuda)
+    inv = orope.inv_freq(1e5, D).to(cuda)
+    msg = "16-byte aligned q, k and v rows"
+    for dtype in (torch.float32, torch.float16):
+        kp = torch.randn(N, bs, KVH, D, generator=g).to(dtype).to(cuda)
+        vp = torch.randn(N, bs, KVH, D, generator=g).to(dtype).to(cuda)
+        wide = torch.randn(B, H * D + 2, generator=g).to(dtype).to(cuda)
+        q_wide = wide.as_strided((B, H, D), (H * D + 2, D, 1))
+        q = q_wide.contiguous()
+        kn = torch.randn(B, KVH, D, generator=g).to(dtype).to(cuda)
+        vn = torch.randn(B, KVH, D, generator=g).to(dtype).to(cuda)
+        assert pkg.decode_attention_supported(q, kp)
+        if dtype == torch.float32:
+            kp0, vp0 = kp.clone(), vp.clone()
+            with pytest.raises(RuntimeError, match=msg):
+                pkg.decode_attention(q_wide, kn, vn, kp, vp, tables, lengths, inv, 35)
+            kbuf = torch.randn(B * KVH * D + 2, generator=g).to(cuda)
+            k_off = kbuf[2:].view(B, KVH, D)
+            with pytest.raises(RuntimeError, match=msg):
+                pkg.decode_attention(q, k_off, vn, kp, vp, tables, lengths, inv, 35)
+            torch.cuda.synchronize()
+            assert torch.equal(kp, kp0) and torch.equal(vp, vp0)
+        else:
+            kp2, vp2 = kp.clone(), vp.clone()
+            a = pkg.decode_attention(q_wide, kn, vn, kp, vp, tables, lengths, inv, 35)
+            b = pkg.decode_attention(q, kn, vn, kp2, vp2, tables, lengths, inv, 35)
+            torch.cuda.synchronize()
+            assert torch.equal(a, b)
+            assert torch.equal(kp, kp2) and torch.equal(vp, vp2)
+    assert pkg.read_device_errors() == 0
