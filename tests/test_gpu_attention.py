@@ -286,15 +286,20 @@ def test_fused_decode_layer_equals_two_launches(pkg, cuda, shape):
     assert pkg.read_device_errors() == 0
 
 
-def test_fused_decode_layer_reads_projection_slices(pkg, cuda):
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_fused_decode_layer_reads_projection_slices(pkg, cuda, dtype):
     """q, k and v given as row slices of one fused q/k/v projection output
     (row stride (H + 2*KVH) * D) give the same output and pool bytes as
-    contiguous copies."""
+    contiguous copies, in FP16 and FP32 (whose slices stay 16-byte aligned:
+    960-float rows, k and v at 576 and 768 floats)."""
     g = torch.Generator().manual_seed(19)
-    w = W.smollm_fp16(batch=48, layers=1)
+    if dtype == torch.float16:
+        w = W.smollm_fp16(batch=48, layers=1)
+    else:
+        w = W.smollm_fp32(batch=48, layers=1)
     t = W.materialize(w, cuda)
     B, H, KVH, D = 48, 9, 3, 64
-    qkv = torch.randn(B, (H + 2 * KVH) * D, generator=g).half().to(cuda)
+    qkv = torch.randn(B, (H + 2 * KVH) * D, generator=g).to(dtype).to(cuda)
     q = qkv[:, :H * D].view(B, H, D)
     k = qkv[:, H * D:(H + KVH) * D].view(B, KVH, D)
     v = qkv[:, (H + KVH) * D:].view(B, KVH, D)
@@ -309,16 +314,19 @@ def test_fused_decode_layer_reads_projection_slices(pkg, cuda):
     assert pkg.read_device_errors() == 0
 
 
-@pytest.mark.parametrize("shape", ["llama3", "smollm"])
+@pytest.mark.parametrize("shape", ["llama3", "smollm", "smollm_fp32"])
 def test_fused_decode_stable_metadata_is_identical(pkg, cuda, shape):
     """A decode step of 4 layers launched back to back with
     metadata_stable=True for layers 1..3 (plan and page lookups before the
     dependent-launch wait) gives the same outputs and pool bytes as the
-    same step without it, eagerly and replayed from a CUDA graph."""
+    same step without it, eagerly and replayed from a CUDA graph; FP16 and
+    FP32 (the SIMT inner loop)."""
     if shape == "llama3":
         w = W.llama3_8b(batch=40, layers=4)
-    else:
+    elif shape == "smollm":
         w = W.smollm_fp16(batch=64, layers=4)
+    else:
+        w = W.smollm_fp32(batch=64, layers=4)
     t = W.materialize(w, cuda)
     pools0 = [(kp.clone(), vp.clone()) for kp, vp in zip(t.k_pools, t.v_pools)]
 
