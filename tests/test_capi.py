@@ -84,6 +84,61 @@ def test_rope_argument_checks(lib):
     assert lib.pdb_rope_kv_write_workspace_size(4, 100, 0) == 0
 
 
+def rope_write(lib, **kw):
+    a = dict(num_slots=8, B=2, S=4, H=4, KVH=2, D=64, N=8, bs=16, dtype=0)
+    a.update(kw)
+    return lib.pdb_rope_kv_write(None, None, None, None, None, None, None, None, 0, 0, None, None,
+                                 None, a["num_slots"], None, a["B"], a["S"], a["H"], a["KVH"],
+                                 a["D"], a["N"], a["bs"], a["dtype"], None, 0, None)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(B=0), "invalid q/k/v shapes"),
+    (dict(S=0), "invalid q/k/v shapes"),
+    (dict(KVH=0), "invalid q/k/v shapes"),
+    (dict(D=63), "head_dim must be even for rotate-half RoPE"),
+    (dict(N=0), "invalid cache shape"),
+    (dict(bs=0), "invalid cache shape"),
+    (dict(dtype=7), "use FP32 or FP16"),
+    (dict(num_slots=7), "number of slots must match the rows written"),
+    (dict(num_slots=-1), "number of slots must match the rows written"),
+    # the kernels index rows in 32 bits
+    (dict(B=1 << 31, S=1, num_slots=1 << 31), "shape too large"),
+    (dict(B=2, S=1 << 30, num_slots=1 << 31), "shape too large"),
+    (dict(), "null tensor pointer"),
+])
+def test_rope_write_argument_checks(lib, kw, msg):
+    """pdb_rope_kv_write validates shapes, slot count and row count (rows are
+    indexed in 32 bits on the device) before any pointer or CUDA call."""
+    assert rope_write(lib, **kw) == 1
+    assert _lib.last_error() == msg
+
+
+def rope_decode(lib, **kw):
+    a = dict(W=4, B=2, H=4, KVH=2, D=64, N=8, bs=16, dtype=0)
+    a.update(kw)
+    return lib.pdb_rope_kv_write_decode(None, None, None, None, None, None, None, None, a["W"],
+                                        None, 0, None, a["B"], a["H"], a["KVH"], a["D"], a["N"],
+                                        a["bs"], a["dtype"], None)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(B=0), "invalid q/k/v shapes"),
+    (dict(D=65), "head_dim must be even for rotate-half RoPE"),
+    (dict(bs=0), "invalid cache shape"),
+    (dict(W=0), "invalid table width"),
+    (dict(dtype=7), "use FP32 or FP16"),
+    (dict(B=1 << 31), "shape too large"),
+    (dict(W=1 << 27, bs=16), "shape too large"),
+    (dict(), "null tensor pointer"),
+])
+def test_rope_decode_argument_checks(lib, kw, msg):
+    """pdb_rope_kv_write_decode validates its shapes, table width and the
+    table's token capacity (positions are formed in 32 bits) first."""
+    assert rope_decode(lib, **kw) == 1
+    assert _lib.last_error() == msg
+
+
 def partition(lib, lengths, kvh, grid):
     lens = np.asarray(lengths, dtype=np.int32)
     ranges = np.zeros(2 * grid, dtype=np.int64)
