@@ -1011,7 +1011,10 @@ int pdb_prefill_attention_impl(const void* q, const void* k_pool, const void* v_
   const bool tc_ok = block_size % pdb::kUnitTokens == 0 && num_blocks * block_size <= INT32_MAX &&
                      batch * width <= INT32_MAX;
   if (impl == PDB_PREFILL_TCGEN05 && !tc_ok)
-    return fail(PDB_ERR_INVALID_ARGUMENT, "the tcgen05 prefill kernel needs block_size % 16 == 0");
+    return fail(PDB_ERR_INVALID_ARGUMENT,
+                block_size % pdb::kUnitTokens
+                    ? "the tcgen05 prefill kernel needs block_size % 16 == 0"
+                    : "the tcgen05 prefill kernel needs under 2^31 pool rows and query rows");
   const bool use_tc = impl == PDB_PREFILL_TCGEN05 || (impl == PDB_PREFILL_AUTO && tc_ok);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

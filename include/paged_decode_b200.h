@@ -332,7 +332,8 @@ PDB_API int pdb_prefill_attention(const void* q, const void* k_pool, const void*
                                   int64_t table_width, int dtype, void* stream);
 
 /* pdb_prefill_attention with the kernel pinned (pdb_prefill_impl_t); same
- * results within FP16 rounding. PDB_PREFILL_TCGEN05 needs block_size % 16 == 0. */
+ * results within FP16 rounding. PDB_PREFILL_TCGEN05 needs block_size % 16 == 0
+ * and num_blocks * block_size and batch * width under 2^31. */
 PDB_API int pdb_prefill_attention_impl(const void* q, const void* k_pool, const void* v_pool,
                                        const int32_t* tables, const int32_t* lengths, void* out,
                                        int64_t batch, int64_t width, int64_t heads,

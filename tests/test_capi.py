@@ -241,6 +241,50 @@ def test_prefill_and_decode_selector_checks(lib):
     assert "requires PDB_DECODE_STABLE_METADATA" in _lib.last_error()
 
 
+def prefill(lib, ptrs=None, **kw):
+    a = dict(B=2, S=40, H=8, D=64, N=64, bs=16, KVH=2, W=4, dtype=1, impl=_lib.PREFILL_AUTO)
+    a.update(kw)
+    p = ptrs or [None] * 6
+    return lib.pdb_prefill_attention_impl(*p, a["B"], a["S"], a["H"], a["D"], a["N"], a["bs"],
+                                          a["KVH"], a["W"], a["dtype"], None, a["impl"])
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(dtype=0), "prefill attention takes FP16"),
+    (dict(B=0), "invalid q shape"),
+    (dict(S=0), "invalid q shape"),
+    (dict(D=96), "prefill attention supports head_dim 64 and 128"),
+    (dict(KVH=3), "query heads must be a multiple of KV heads"),
+    (dict(W=0), "invalid cache shape"),
+    (dict(bs=0), "invalid cache shape"),
+    (dict(B=65536), "shape too large"),
+    (dict(S=64 * 65535 + 1), "shape too large"),
+    (dict(), "null tensor pointer"),
+])
+def test_prefill_argument_checks(lib, kw, msg):
+    """pdb_prefill_attention_impl validates dtype, shapes, head_dim, the head
+    grouping, the cache shape and the grid limits before its pointers."""
+    assert prefill(lib, **kw) == 1
+    assert _lib.last_error() == msg
+
+
+@pytest.mark.skipif(torch.cuda.is_available(),
+                    reason="uses made-up addresses: host-only checks, never a GPU")
+@pytest.mark.parametrize("kw,ptrs,msg", [
+    (dict(), [16, 8, 32, 48, 64, 80], "tensors must be 16-byte aligned"),
+    (dict(bs=8, impl=_lib.PREFILL_TCGEN05), [16] * 6,
+     "the tcgen05 prefill kernel needs block_size % 16 == 0"),
+    (dict(N=1 << 27, impl=_lib.PREFILL_TCGEN05), [16] * 6,
+     "the tcgen05 prefill kernel needs under 2^31 pool rows and query rows"),
+])
+def test_prefill_pointer_and_kernel_checks(lib, kw, ptrs, msg):
+    """Past the null check: unaligned tensors, and a pinned tcgen05 kernel
+    outside its block-size and row-count limits, are rejected on the host
+    (the addresses are never dereferenced; no CUDA call is made)."""
+    assert prefill(lib, ptrs, **kw) == 1
+    assert _lib.last_error() == msg
+
+
 def test_prefill_ops_checks_without_device(pkg):
     """prefill_attention rejects CPU tensors before reaching the library."""
     q = torch.zeros(1, 4, 2, 64, dtype=torch.float16)
