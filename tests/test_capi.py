@@ -285,6 +285,48 @@ def test_prefill_pointer_and_kernel_checks(lib, kw, ptrs, msg):
     assert _lib.last_error() == msg
 
 
+def attn_impl(lib, ptrs=None, impl=0, **kw):
+    a = dict(B=2, H=4, D=32, N=12, bs=16, KVH=2, Dk=32, W=3, max_length=35, dtype=0)
+    a.update(kw)
+    p = ptrs or [None] * 6
+    return lib.pdb_paged_attention_impl(*p, a["B"], a["H"], a["D"], a["N"], a["bs"], a["KVH"],
+                                        a["Dk"], a["W"], a["max_length"], a["dtype"], None, 0,
+                                        None, impl)
+
+
+def test_attention_impl_and_wrappers_checks(lib):
+    """The kernel-pinned attention entry point and the decode / prefill
+    wrappers run the same argument checks as the entry points they share
+    them with; the support query rejects invalid shapes on any device."""
+    assert attn_impl(lib, dtype=7) == 1 and _lib.last_error() == "use FP32 or FP16"
+    assert attn_impl(lib, KVH=3) == 1
+    assert _lib.last_error() == "query heads must be a multiple of KV heads"
+    assert attn_impl(lib) == 1 and _lib.last_error() == "null tensor pointer"
+    dec = [None] * 9 + [2, 4, 64, 16, 16, 2, 1, 16, 0, 0]
+    assert lib.pdb_decode_attention(*dec, 7, None, 0, None) == 1
+    assert _lib.last_error() == "use FP32 or FP16"
+    assert lib.pdb_decode_attention(*dec, 1, None, 0, None) == 1
+    assert _lib.last_error() == "null tensor pointer"
+    pre = [None] * 6 + [2, 8, 4, 64, 16, 16, 2, 1]
+    assert lib.pdb_prefill_attention(*pre, 0, None) == 1
+    assert _lib.last_error() == "prefill attention takes FP16"
+    assert lib.pdb_prefill_attention(*pre, 1, None) == 1
+    assert _lib.last_error() == "null tensor pointer"
+    for args in [(64, 9, 3, 64, 4096, 16, 7), (0, 9, 3, 64, 4096, 16, 1),
+                 (64, 9, 0, 64, 4096, 16, 1), (64, 9, 2, 64, 4096, 16, 1)]:
+        assert lib.pdb_decode_attention_supported(*args) == 0
+
+
+@pytest.mark.skipif(torch.cuda.is_available(),
+                    reason="uses made-up addresses: host-only checks, never a GPU")
+@pytest.mark.parametrize("impl", [-1, _lib.IMPL_TMA_STATIC + 1])
+def test_attention_unknown_kernel_selection(lib, impl):
+    """An unknown kernel selector is rejected after the pointer checks, before
+    any CUDA call (the addresses are never dereferenced)."""
+    assert attn_impl(lib, [16] * 6, impl) == 1
+    assert _lib.last_error() == "unknown kernel selection"
+
+
 def test_prefill_ops_checks_without_device(pkg):
     """prefill_attention rejects CPU tensors before reaching the library."""
     q = torch.zeros(1, 4, 2, 64, dtype=torch.float16)
